@@ -1,0 +1,179 @@
+"""Python access to the CPU oracle (oracle/liboracle.so) -- TEST INFRASTRUCTURE ONLY.
+
+This module is the checker for the CUDA path.  Only tests/, __graft_entry__.smoke() and
+bench.py's cpu_baseline / reference leg import it; the shipped package (blackhole_b200)
+never does.  The C code it wraps restates the reference's host path
+(example/nvfp4_bf16_gemm.cu:60-71 and :161-168, include/blackhole/sm120/nvfp4_gemm.hpp:293-302);
+see oracle/nvfp4_oracle.h.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+REF_SHIM_PATH = os.path.join(HERE, "_ref", "libref_shim.so")
+
+_lib = None
+_ref = None
+
+c_i64 = ctypes.c_int64
+c_ptr = ctypes.c_void_p
+
+
+def build(force: bool = False) -> None:
+    """Compile liboracle.so (gcc) if it is missing or stale."""
+    src = os.path.join(HERE, "nvfp4_oracle.c")
+    if force or not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < os.path.getmtime(src):
+        subprocess.check_call(["make", "-s", "-C", HERE, "liboracle.so"])
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        build()
+        L = ctypes.CDLL(LIB_PATH)
+        L.bho_e2m1_from_float.restype = ctypes.c_uint8
+        L.bho_e2m1_from_float.argtypes = [ctypes.c_float]
+        L.bho_e2m1_to_float.restype = ctypes.c_float
+        L.bho_e2m1_to_float.argtypes = [ctypes.c_uint8]
+        L.bho_ue4m3_from_float.restype = ctypes.c_uint8
+        L.bho_ue4m3_from_float.argtypes = [ctypes.c_float]
+        L.bho_ue4m3_to_float.restype = ctypes.c_float
+        L.bho_ue4m3_to_float.argtypes = [ctypes.c_uint8]
+        L.bho_bf16_from_float.restype = ctypes.c_uint16
+        L.bho_bf16_from_float.argtypes = [ctypes.c_float]
+        L.bho_sf_offset.restype = c_i64
+        L.bho_sf_offset.argtypes = [c_i64, c_i64, c_i64]
+        L.bho_sf_storage_bytes.restype = c_i64
+        L.bho_sf_storage_bytes.argtypes = [c_i64, c_i64]
+        L.bho_gen_normal.restype = None
+        L.bho_gen_normal.argtypes = [ctypes.c_uint64, c_i64, c_i64, ctypes.c_float, ctypes.c_float, c_ptr]
+        L.bho_apply_outliers.restype = None
+        L.bho_apply_outliers.argtypes = [ctypes.c_uint64, c_i64, ctypes.c_double, ctypes.c_float, c_ptr]
+        L.bho_quantize_nvfp4.restype = ctypes.c_float
+        L.bho_quantize_nvfp4.argtypes = [c_ptr, c_i64, c_i64, c_ptr, c_ptr]
+        L.bho_gemm_ref_full.restype = None
+        L.bho_gemm_ref_full.argtypes = [c_i64, c_i64, c_i64, c_ptr, c_ptr, c_ptr, c_ptr,
+                                        ctypes.c_float, c_ptr, c_ptr, ctypes.c_int]
+        L.bho_gemm_ref_sampled.restype = None
+        L.bho_gemm_ref_sampled.argtypes = [c_i64, c_i64, c_i64, c_ptr, c_ptr, c_ptr, c_ptr,
+                                           ctypes.c_float, c_i64, c_ptr, c_ptr, c_ptr, c_ptr,
+                                           ctypes.c_int]
+        L.bho_tolerance.restype = ctypes.c_double
+        L.bho_tolerance.argtypes = [ctypes.c_float, ctypes.c_float, ctypes.c_float, c_i64, ctypes.c_double]
+        _lib = L
+    return _lib
+
+
+def ref_shim():
+    """The reference-backed shim (oracle/_ref), or None when it was not built."""
+    global _ref
+    if _ref is None and os.path.exists(REF_SHIM_PATH):
+        R = ctypes.CDLL(REF_SHIM_PATH)
+        R.ref_sf_offset.restype = c_i64
+        R.ref_sf_offset.argtypes = [c_i64, c_i64, c_i64, c_i64, ctypes.c_int]
+        R.ref_sf_cosize.restype = c_i64
+        R.ref_sf_cosize.argtypes = [c_i64, c_i64, ctypes.c_int]
+        R.ref_e2m1.restype = ctypes.c_uint8
+        R.ref_e2m1.argtypes = [ctypes.c_float]
+        R.ref_ue4m3.restype = ctypes.c_uint8
+        R.ref_ue4m3.argtypes = [ctypes.c_float]
+        R.ref_bf16.restype = ctypes.c_uint16
+        R.ref_bf16.argtypes = [ctypes.c_float]
+        _ref = R
+    return _ref
+
+
+def _p(a: np.ndarray):
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(c_ptr)
+
+
+# ---- vectorised helpers (numpy in, numpy out) -------------------------------------------
+
+def sf_storage_bytes(mn: int, k: int) -> int:
+    return int(lib().bho_sf_storage_bytes(mn, k))
+
+
+def sf_offset(mn: int, kg: int, k: int) -> int:
+    return int(lib().bho_sf_offset(mn, kg, k))
+
+
+def sf_offsets(mn: int, k: int) -> np.ndarray:
+    """Offsets for every (row, k-group) of an (mn, k) tensor, same rule as the C code."""
+    kgb = (k // 16 + 3) // 4
+    r = np.arange(mn, dtype=np.int64)[:, None]
+    g = np.arange(k // 16, dtype=np.int64)[None, :]
+    return ((r // 128) * kgb + g // 4) * 512 + (r % 32) * 16 + ((r // 32) % 4) * 4 + (g % 4)
+
+
+def gen_normal(seed: int, n: int, mean: float = 0.0, std: float = 1.0, offset: int = 0) -> np.ndarray:
+    out = np.empty(n, dtype=np.float32)
+    lib().bho_gen_normal(seed, offset, n, mean, std, _p(out))
+    return out
+
+
+def apply_outliers(seed: int, x: np.ndarray, p: float, factor: float) -> None:
+    lib().bho_apply_outliers(seed, x.size, p, factor, _p(x))
+
+
+def quantize(X: np.ndarray):
+    """NVFP4-quantise a (rows, K) float32 matrix: returns (packed u8, sf u8, global_scale)."""
+    X = np.ascontiguousarray(X, dtype=np.float32)
+    rows, k = X.shape
+    packed = np.zeros(rows * k // 2, dtype=np.uint8)
+    sf = np.zeros(sf_storage_bytes(rows, k), dtype=np.uint8)
+    g = lib().bho_quantize_nvfp4(_p(X), rows, k, _p(packed), _p(sf))
+    return packed, sf, float(g)
+
+
+def gemm_full(M, N, K, A, SFA, B, SFB, alpha=1.0, nthreads=0, want_absdot=True):
+    """Full host reference: returns (D bf16 bits as uint16 [M,N], absdot [M,N] or None)."""
+    D = np.empty((M, N), dtype=np.uint16)
+    ad = np.empty((M, N), dtype=np.float64) if want_absdot else None
+    nt = nthreads if nthreads > 0 else (os.cpu_count() or 1)
+    lib().bho_gemm_ref_full(M, N, K, _p(A), _p(SFA), _p(B), _p(SFB), alpha, _p(D),
+                            _p(ad) if ad is not None else None, nt)
+    return D, ad
+
+
+def gemm_sampled(M, N, K, A, SFA, B, SFB, ms, ns, alpha=1.0, nthreads=0):
+    ms = np.ascontiguousarray(ms, dtype=np.int64)
+    ns = np.ascontiguousarray(ns, dtype=np.int64)
+    S = ms.size
+    D = np.empty(S, dtype=np.uint16)
+    ad = np.empty(S, dtype=np.float64)
+    nt = nthreads if nthreads > 0 else (os.cpu_count() or 1)
+    lib().bho_gemm_ref_sampled(M, N, K, _p(A), _p(SFA), _p(B), _p(SFB), alpha, S,
+                               _p(ms), _p(ns), _p(D), _p(ad), nt)
+    return D, ad
+
+
+def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
+    return (bits.astype(np.uint32) << 16).view(np.float32)
+
+
+def tolerance(ref: np.ndarray, got: np.ndarray, alpha: float, K: int, absdot: np.ndarray) -> np.ndarray:
+    """Vectorised form of bho_tolerance: ulp_bf16(max|.|) + |alpha|*K*2^-24*absdot."""
+    a = np.maximum(np.abs(ref.astype(np.float64)), np.abs(got.astype(np.float64)))
+    a = np.maximum(a, np.float64(np.finfo(np.float32).tiny))
+    _, e = np.frexp(a)
+    ulp = np.ldexp(1.0, (e - 1) - 7)
+    return ulp + abs(alpha) * K * 2.0 ** -24 * absdot
+
+
+def check(ref_bits: np.ndarray, got_bits: np.ndarray, alpha: float, K: int, absdot: np.ndarray):
+    """Returns (n_bad, max_abs_err, max_err_over_tol, reference_rel_max) for BF16 outputs."""
+    ref = bf16_bits_to_f32(ref_bits.ravel())
+    got = bf16_bits_to_f32(got_bits.ravel())
+    err = np.abs(ref.astype(np.float64) - got.astype(np.float64))
+    tol = tolerance(ref, got, alpha, K, absdot.ravel())
+    bad = int(np.count_nonzero(~(err <= tol)))
+    # the reference example's own check: |got-ref|/(|ref|+1e-3) <= 0.05 (example:169-172)
+    rel = err / (np.abs(ref.astype(np.float64)) + 1e-3)
+    return bad, float(err.max(initial=0.0)), float((err / tol).max(initial=0.0)), float(rel.max(initial=0.0))
