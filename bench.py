@@ -1,0 +1,429 @@
+#!/usr/bin/env python3
+"""Benchmark of the sm_100a NVFP4 x NVFP4 -> BF16 GEMM (one JSON line on rank 0).
+
+Workload: M = N = K = 8192, A and B drawn from N(0,1) on the device
+(seeded torch generator), quantised to NVFP4 by this library's GPU quantiser (global scale
+amax/(448*6), per-16 UE4M3 block scales, E2M1 RNE), alpha = gA*gB, BF16 output.
+With --gpus P > 1 the GEMM is split along N: every rank owns an 8192-column slice of B
+(weak scaling: global N = 8192*P) and A is replicated; no collective sits on the data path.
+The optional NCCL all-gather of the C slices is timed separately ("gather").
+
+A "step" is one GEMM launch.  `value` = whole-job TFLOP/s from CUDA events around each
+launch (max over ranks), L2 flushed (256 MB write) before every timed launch.  `e2e` is the
+same GEMM through the C ABI with pinned host buffers: H2D of A/SFA/B/SFB and D2H of D
+inside the timed region.  The decode shape (configs[2], M=16 N=28672 K=8192) is reported
+under "decode" in HBM GB/s.
+
+--impl reference runs the reference's host GEMM (the CPU oracle's restatement of
+example/nvfp4_bf16_gemm.cu:161-168) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+SPEC_FP4_TFLOPS = 9000.0      # B200 dense FP4 (4 x the 2250 TF/s dense BF16 figure)
+SPEC_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0     # used only when the measured-peaks file is absent
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--m", type=int, default=8192)
+    ap.add_argument("--n", type=int, default=8192, help="columns per GPU")
+    ap.add_argument("--k", type=int, default=8192)
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--gather", action="store_true", help="also time the NCCL all-gather (P>1)")
+    return ap.parse_args()
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(path))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def profiled_traffic(key):
+    """DRAM bytes per launch from a committed ncu capture (profiles/traffic.json)."""
+    try:
+        return json.load(open(os.path.join(ROOT, "profiles", "traffic.json")))[key]["bytes_per_launch"]
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------------------------------
+# clocks during the timed region (NVML, the library behind nvidia-smi)
+# ---------------------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+               "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
+
+    def __init__(self, device_index, interval=0.02):
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thr = None
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            self.nv = nv
+            self.h = nv.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+        self.interval = interval
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for name, bit in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.interval)
+
+    def __enter__(self):
+        if self.nv is not None:
+            self._thr = threading.Thread(target=self._run, daemon=True)
+            self._thr.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._thr:
+            self._thr.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------------------
+def dist_setup(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    import torch
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+# ---------------------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------------------
+def make_operand(rows, K, seed, std, dev):
+    import torch
+    import blackhole_b200 as bh
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    x = torch.randn((rows, K), generator=g, device=dev, dtype=torch.float32)
+    if std != 1.0:
+        x.mul_(std)
+    packed, sf, scales = bh.quantize_tensor(x)
+    torch.cuda.synchronize()
+    del x
+    return packed, sf, scales
+
+
+def gemm_bytes(M, N, K):
+    return M * K // 2 + N * K // 2 + M * K // 16 + N * K // 16 + 2 * M * N
+
+
+def time_gemm(M, N, K, A, SFA, B, SFB, D, alpha, steps, warmup, flush, world):
+    """Per-launch CUDA-event times (ms) on the current stream, L2 flushed before each."""
+    import torch
+    import blackhole_b200 as bh
+
+    stream = torch.cuda.current_stream()
+    for _ in range(warmup):
+        bh.nvfp4_bf16_gemm(M, N, K, A, SFA, B, SFB, D, alpha)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    barrier(world)
+    for s, e in ev:
+        flush.zero_()
+        s.record(stream)
+        bh.nvfp4_bf16_gemm(M, N, K, A, SFA, B, SFB, D, alpha)
+        e.record(stream)
+    barrier(world)
+    return [s.elapsed_time(e) for s, e in ev]
+
+
+def run_e2e(M, N, K, A, SFA, B, SFB, alpha, steps, world):
+    """C-ABI call with pinned host buffers; H2D inputs and D2H output inside the region."""
+    import torch
+    import blackhole_b200 as bh
+
+    dev = A.device
+    hA, hSFA, hB, hSFB = (t.cpu().pin_memory() for t in (A, SFA, B, SFB))
+    dA, dSFA, dB, dSFB = (torch.empty_like(t) for t in (A, SFA, B, SFB))
+    dD = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    hD = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
+    stream = torch.cuda.current_stream()
+    h2d = sum(t.numel() * t.element_size() for t in (hA, hSFA, hB, hSFB))
+    d2h = hD.numel() * hD.element_size()
+
+    def step():
+        dA.copy_(hA, non_blocking=True)
+        dSFA.copy_(hSFA, non_blocking=True)
+        dB.copy_(hB, non_blocking=True)
+        dSFB.copy_(hSFB, non_blocking=True)
+        bh.nvfp4_bf16_gemm(M, N, K, dA, dSFA, dB, dSFB, dD, alpha)
+        hD.copy_(dD, non_blocking=True)
+
+    step()
+    barrier(world)
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(steps):
+        step()
+    e.record(stream)
+    barrier(world)
+    ms = s.elapsed_time(e) / steps
+    return ms, h2d, d2h
+
+
+# ---------------------------------------------------------------------------------------
+# CPU legs (the oracle restatement of the reference's host loop)
+# ---------------------------------------------------------------------------------------
+def cpu_reference_rows(A, SFA, B, SFB, N, K, rows, threads, alpha):
+    """Reference host GEMM on `rows` full output rows (all N columns); returns seconds."""
+    from oracle import oracle as O
+    t0 = time.perf_counter()
+    O.gemm_full(rows, N, K, A, SFA, B, SFB, alpha=alpha, nthreads=threads, want_absdot=False)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(A, SFA, B, SFB, N, K, alpha, budget_s=12.0):
+    threads = os.cpu_count() or 1
+    # calibrate on a small slice, then size the sample to the time budget
+    cols = min(N, 1024)
+    t = cpu_reference_rows(A, SFA, B[: cols * K // 2], SFB, cols, K, threads, threads, alpha)
+    per_mac = t / (threads * cols * K)
+    rows = max(threads, min(128, int(budget_s / (per_mac * N * K) / threads) * threads))
+    t = cpu_reference_rows(A, SFA, B, SFB, N, K, rows, threads, alpha)
+    tflops = 2.0 * rows * N * K / t / 1e12
+    return {"value": tflops, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{rows} full output rows x N={N} x K={K} of the host reference loop "
+                      f"(sequential FP32 dot, example/nvfp4_bf16_gemm.cu:161-168), "
+                      f"{threads} threads, {t:.1f} s; TFLOP/s = 2*rows*N*K/t"}
+
+
+def reference_arm(args, world, rank):
+    """--impl reference: the reference's host GEMM on the host cores, rank 0 only."""
+    import numpy as np
+    from oracle import oracle as O
+
+    if rank != 0:
+        return None
+    M, N, K = args.m, args.n, args.k
+    threads = os.cpu_count() or 1
+    # Inputs: the same recipe on the host (seeded), only the rows/columns a step touches.
+    cols = min(N, 2048)
+    xa = O.gen_normal(1, threads * K).reshape(threads, K)
+    xb = O.gen_normal(2, cols * K).reshape(cols, K)
+    A, SFA, ga = O.quantize(xa)
+    B, SFB, gb = O.quantize(xb)
+    alpha = float(np.float32(ga) * np.float32(gb))
+    # per-step sample: `threads` rows x `cols` columns x K, sized so the run stays short
+    t_one = cpu_reference_rows(A, SFA, B, SFB, cols, K, threads, threads, alpha)
+    total_steps = args.steps + args.warmup
+    budget = 90.0
+    if t_one * total_steps > budget:
+        cols = max(128, int(cols * budget / (t_one * total_steps)) // 128 * 128)
+    for _ in range(args.warmup):
+        cpu_reference_rows(A, SFA, B, SFB, cols, K, threads, threads, alpha)
+    times = []
+    for _ in range(args.steps):
+        times.append(cpu_reference_rows(A, SFA, B, SFB, cols, K, threads, threads, alpha))
+    t = sum(times)
+    flops = 2.0 * threads * cols * K * args.steps
+    v = flops / t / 1e12
+    sample = (f"{threads} output rows x {cols} columns x K={K} per step of the host reference "
+              f"loop (example/nvfp4_bf16_gemm.cu:161-168), {threads} threads")
+    return {
+        "metric": "NVFP4 GEMM TFLOPS @8192^3 (% FP4 peak); M=16 decode GEMM HBM GB/s",
+        "impl": "reference", "value": v, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic", "config": {"workload": f"nvfp4 gemm M={M} N={N} K={K} (sampled on CPU)"},
+        "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+# ---------------------------------------------------------------------------------------
+def main():
+    args = parse()
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        out = reference_arm(args, world, rank)
+        if out is not None:
+            print(json.dumps(out), flush=True)
+        return
+
+    import torch
+    import blackhole_b200 as bh
+
+    world, rank, local = dist_setup(args)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    hbm_peak, bf16_peak, peak_src = measured_peaks()
+    fp4_peak = 4.0 * bf16_peak
+    M, N, K = args.m, args.n, args.k
+
+    A, SFA, scA = make_operand(M, K, 1, 1.0, dev)                 # replicated (seed 1)
+    B, SFB, scB = make_operand(N, K, 1000 + rank, 1.0, dev)       # this rank's N slice
+    alpha = float(scA[1].item() * scB[1].item())
+    D = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.int32, device=dev)
+
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        times = time_gemm(M, N, K, A, SFA, B, SFB, D, alpha, args.steps, args.warmup, flush, world)
+    assert bh.device_status(torch.cuda.current_device()) == 0
+    total_ms = max_over_ranks(sum(times), world)
+    ms_step = total_ms / args.steps
+    flops_rank = 2.0 * M * N * K
+    value = flops_rank * world * args.steps / (total_ms * 1e-3) / 1e12
+    achieved = flops_rank / (statistics.mean(times) * 1e-3) / 1e12
+
+    result = {
+        "metric": "NVFP4 GEMM TFLOPS @8192^3 (% FP4 peak); M=16 decode GEMM HBM GB/s",
+        "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4",
+        "data": "synthetic: N(0,1) via seeded torch.randn on device, NVFP4-quantised on device",
+        "config": {"workload": f"nvfp4 gemm M={M} N={N}/gpu K={K} (BASELINE configs[1]; N-split "
+                               f"across {world} GPU(s), A replicated)",
+                   "M": M, "N_per_gpu": N, "N_total": N * world, "K": K,
+                   "parallelism": f"n-split{world}", "l2": "flushed (256 MB write) before each launch"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s",
+                     "frac": achieved / fp4_peak,
+                     "peak_source": f"4 x {peak_src} dense bf16 ({bf16_peak} TF/s); FP4 dense = 4x BF16 per SM-clock",
+                     "frac_of_spec_9pf": achieved / SPEC_FP4_TFLOPS,
+                     "traffic": profiled_traffic(f"gemm_{M}x{N}x{K}")},
+        "gpu_launches": args.steps,
+    }
+
+    if not args.no_decode:
+        Md, Nd, Kd = 16, 28672, 8192
+        Ad, SFAd, scAd = make_operand(Md, Kd, 2, 1.0, dev)
+        Bd, SFBd, scBd = make_operand(Nd, Kd, 2000 + rank, 0.02, dev)
+        Dd = torch.empty((Md, Nd), dtype=torch.bfloat16, device=dev)
+        alpha_d = float(scAd[1].item() * scBd[1].item())
+        dsteps = max(20, args.steps)
+        dt = time_gemm(Md, Nd, Kd, Ad, SFAd, Bd, SFBd, Dd, alpha_d, dsteps, args.warmup, flush, world)
+        dms = max_over_ranks(statistics.mean(dt), world)
+        nbytes = gemm_bytes(Md, Nd, Kd)
+        gbs = nbytes / (dms * 1e-3) / 1e9
+        result["decode"] = {"workload": f"M={Md} N={Nd} K={Kd} (BASELINE configs[2]) per GPU",
+                            "value": gbs * world, "unit": "GB/s", "ms_per_step": dms,
+                            "bytes_per_launch": nbytes, "roofline_frac": gbs / hbm_peak,
+                            "peak": hbm_peak, "peak_source": peak_src,
+                            "frac_of_spec_8tbs": gbs / SPEC_HBM_GBS, "steps": dsteps,
+                            "traffic": profiled_traffic(f"gemm_{Md}x{Nd}x{Kd}")}
+        result["gpu_launches"] += dsteps
+        del Ad, Bd, SFAd, SFBd, Dd
+
+    if world > 1 and args.gather:
+        import torch.distributed as dist
+        out = torch.empty((world, M, N), dtype=torch.bfloat16, device=dev)
+        for _ in range(3):
+            dist.all_gather_into_tensor(out, D)
+        barrier(world)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(10):
+            dist.all_gather_into_tensor(out, D)
+        e.record()
+        barrier(world)
+        gms = max_over_ranks(s.elapsed_time(e) / 10, world)
+        result["gather"] = {"ms_per_step": gms, "layout": "[P][M][N/P] bf16",
+                            "bytes_per_gpu_in": (world - 1) * M * N * 2,
+                            "with_gather_tflops": flops_rank * world / ((ms_step + gms) * 1e-3) / 1e12}
+        del out
+
+    if not args.no_e2e:
+        esteps = max(3, min(args.steps, 20))
+        ems, h2d, d2h = run_e2e(M, N, K, A, SFA, B, SFB, alpha, esteps, world)
+        ems = max_over_ranks(ems, world)
+        result["e2e"] = {"value": flops_rank * world / (ems * 1e-3) / 1e12, "unit": "TFLOP/s",
+                         "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                         "ms_per_step": ems, "steps": esteps,
+                         "path": "blackhole_sm100_nvfp4_bf16_gemm (C ABI) + pinned host copies"}
+        result["gpu_launches"] += esteps + 1
+
+    result["clocks"] = clk.summary()
+
+    if rank == 0 and world == 1 and not args.no_cpu:
+        hA = A.cpu().numpy().reshape(-1)
+        hSFA = SFA.cpu().numpy()
+        hB = B.cpu().numpy().reshape(-1)
+        hSFB = SFB.cpu().numpy()
+        result["cpu_baseline"] = cpu_baseline(hA, hSFA, hB, hSFB, N, K, alpha)
+
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,154 @@
+"""blackhole_b200 -- B200 (sm_100a) NVFP4 x NVFP4 -> BF16 block-scaled GEMM.
+
+Python mirror of the reference operator call ``blackhole::sm120::nvfp4_bf16_gemm``
+(include/blackhole/sm120/nvfp4_gemm.hpp:588-637) over the C ABI in
+include/blackhole_sm100.h.  Device memory may be passed as torch tensors (any dtype,
+contiguous, on a CUDA device) or as raw integer device pointers.
+
+There is no fallback: if libblackhole_sm100.so is missing or fails to load, every call
+raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+__all__ = [
+    "LIB_PATH", "load", "nvfp4_bf16_gemm", "sf_storage_bytes", "sf_offset",
+    "device_status", "BlackholeError", "nvfp4_quantize", "quantize_tensor",
+]
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libblackhole_sm100.so")
+
+_lib = None
+
+
+class BlackholeError(RuntimeError):
+    """A C-ABI call returned a CUDA error code."""
+
+    def __init__(self, fn: str, code: int):
+        super().__init__(f"{fn} failed with cudaError {code} ({_CUDA_ERRORS.get(code, 'error')})")
+        self.code = code
+
+
+_CUDA_ERRORS = {0: "cudaSuccess", 1: "cudaErrorInvalidValue", 2: "cudaErrorMemoryAllocation",
+                98: "cudaErrorInvalidDeviceFunction", 101: "cudaErrorInvalidDevice",
+                209: "cudaErrorNoKernelImageForDevice", 400: "cudaErrorInvalidResourceHandle",
+                700: "cudaErrorIllegalAddress", 801: "cudaErrorNotSupported"}
+
+
+def load():
+    """Load libblackhole_sm100.so (raises if it is absent: no fallback path exists)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is missing; build it with `python blackhole_b200/build.py`")
+    L = ctypes.CDLL(LIB_PATH)
+    vp, i32, i64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
+    L.blackhole_sm100_nvfp4_bf16_gemm.restype = i32
+    L.blackhole_sm100_nvfp4_bf16_gemm.argtypes = [i32, i32, i32, vp, vp, vp, vp, vp, ctypes.c_float, vp]
+    L.blackhole_sm100_sf_storage_bytes.restype = i64
+    L.blackhole_sm100_sf_storage_bytes.argtypes = [i64, i64]
+    L.blackhole_sm100_sf_offset.restype = i64
+    L.blackhole_sm100_sf_offset.argtypes = [i64, i64, i64]
+    L.blackhole_sm100_device_status.restype = i32
+    L.blackhole_sm100_device_status.argtypes = [i32, ctypes.POINTER(ctypes.c_uint), i32]
+    L.blackhole_sm100_nvfp4_quantize.restype = i32
+    L.blackhole_sm100_nvfp4_quantize.argtypes = [vp, i32, i32, i32, vp, vp, vp, vp]
+    L.blackhole_sm100_abi_version.restype = i32
+    L.blackhole_sm100_abi_version.argtypes = []
+    _lib = L
+    return L
+
+
+def _ptr(x) -> int:
+    if x is None:
+        return 0
+    if isinstance(x, int):
+        return x
+    if hasattr(x, "data_ptr"):
+        if hasattr(x, "is_cuda") and not x.is_cuda:
+            raise ValueError("tensor must live on a CUDA device")
+        if hasattr(x, "is_contiguous") and not x.is_contiguous():
+            raise ValueError("tensor must be contiguous")
+        return int(x.data_ptr())
+    raise TypeError(f"cannot take a device pointer from {type(x)!r}")
+
+
+def _stream(stream) -> int:
+    if stream is None:
+        try:
+            import torch
+            return int(torch.cuda.current_stream().cuda_stream)
+        except Exception:
+            return 0
+    if isinstance(stream, int):
+        return stream
+    return int(stream.cuda_stream)
+
+
+def nvfp4_bf16_gemm(M: int, N: int, K: int, A, SFA, B, SFB, D, alpha: float = 1.0, stream=None) -> None:
+    """D = bf16(alpha * A . B^T) for NVFP4 operands (asynchronous on `stream`).
+
+    Same arguments as the reference call, in the same order, plus alpha:
+    A (M x K/2 bytes, E2M1 packed, low nibble = even k), SFA (UE4M3, 128x4 layout,
+    sf_storage_bytes(M, K) bytes), B (N x K/2), SFB, D (M x N bf16, row-major).
+    Raises BlackholeError(cudaErrorInvalidValue) for unsupported shapes
+    (M >= 1, N % 128 == 0, K % 256 == 0), null or misaligned pointers.
+    """
+    rc = load().blackhole_sm100_nvfp4_bf16_gemm(
+        int(M), int(N), int(K), _ptr(A), _ptr(SFA), _ptr(B), _ptr(SFB), _ptr(D),
+        float(alpha), _stream(stream))
+    if rc != 0:
+        raise BlackholeError("blackhole_sm100_nvfp4_bf16_gemm", rc)
+
+
+def sf_storage_bytes(mn: int, k: int) -> int:
+    """Bytes of a (mn x k) scale-factor tensor in the 128x4 layout (padding included)."""
+    return int(load().blackhole_sm100_sf_storage_bytes(int(mn), int(k)))
+
+
+def sf_offset(mn: int, kg: int, k: int) -> int:
+    return int(load().blackhole_sm100_sf_offset(int(mn), int(kg), int(k)))
+
+
+def device_status(device: int = 0, clear: bool = True) -> int:
+    """Status bits of this library's kernels on `device` (0 = no pipeline timed out).
+
+    Synchronises the device."""
+    out = ctypes.c_uint(0)
+    rc = load().blackhole_sm100_device_status(int(device), ctypes.byref(out), 1 if clear else 0)
+    if rc != 0:
+        raise BlackholeError("blackhole_sm100_device_status", rc)
+    return int(out.value)
+
+
+
+def nvfp4_quantize(X, rows: int, K: int, packed, sf, scales, x_is_bf16: bool = False, stream=None) -> None:
+    """Quantise X (rows x K, FP32 or BF16) to NVFP4 on the GPU (asynchronous).
+
+    Writes packed E2M1 (rows*K/2 bytes), UE4M3 scale factors in the 128x4 layout
+    (sf_storage_bytes(rows, K) bytes) and scales = [amax, g] (device float32[2])."""
+    rc = load().blackhole_sm100_nvfp4_quantize(
+        _ptr(X), 1 if x_is_bf16 else 0, int(rows), int(K), _ptr(packed), _ptr(sf), _ptr(scales),
+        _stream(stream))
+    if rc != 0:
+        raise BlackholeError("blackhole_sm100_nvfp4_quantize", rc)
+
+
+def quantize_tensor(X, stream=None):
+    """Convenience wrapper for a 2-D torch tensor (float32 or bfloat16) on a CUDA device.
+
+    Returns (packed uint8 [rows, K/2], sf uint8 [sf_storage_bytes], scales float32 [2])."""
+    import torch
+
+    if X.dim() != 2 or X.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("X must be a 2-D float32 or bfloat16 tensor")
+    rows, K = X.shape
+    packed = torch.empty((rows, K // 2), dtype=torch.uint8, device=X.device)
+    sf = torch.empty(sf_storage_bytes(rows, K), dtype=torch.uint8, device=X.device)
+    scales = torch.empty(2, dtype=torch.float32, device=X.device)
+    nvfp4_quantize(X, rows, K, packed, sf, scales, x_is_bf16=(X.dtype == torch.bfloat16), stream=stream)
+    return packed, sf, scales

@@ -1,0 +1,77 @@
+/*
+ * blackhole_sm100.h -- C ABI of the B200 (sm_100a) NVFP4 x NVFP4 -> BF16 GEMM.
+ *
+ * Exported by blackhole_b200/libblackhole_sm100.so.  Plain pointers and sizes only; every
+ * buffer is caller-owned device memory and every call is asynchronous on `stream`.
+ * Return values are cudaError_t codes (0 = cudaSuccess).
+ */
+#ifndef BLACKHOLE_SM100_H
+#define BLACKHOLE_SM100_H
+
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BLACKHOLE_SM100_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define BLACKHOLE_SM100_API __attribute__((visibility("default")))
+#else
+#define BLACKHOLE_SM100_API
+#endif
+
+/* D = bf16(alpha * A . B^T), block-scaled NVFP4 operands.
+ *
+ * Replaces blackhole::sm120::nvfp4_bf16_gemm(M, N, K, A_packed, SFA, B_packed, SFB, D,
+ * stream) of the reference (include/blackhole/sm120/nvfp4_gemm.hpp:588-591); the argument
+ * meanings are the reference's (nvfp4_gemm.hpp:583-587):
+ *   A   : E2M1, M x K, K-contiguous, two per byte, even k in the low nibble
+ *   SFA : UE4M3 scale factors of A in the 128x4 blocked layout (make_layout_SFA(M, K))
+ *   B   : E2M1, N x K, K-contiguous
+ *   SFB : UE4M3 scale factors of B (make_layout_SFB(N, K))
+ *   D   : BF16, M x N, row-major
+ * plus `alpha`, the product of the two global scales (alpha = 1 reproduces the reference).
+ * Shapes: M >= 1, N % 128 == 0, K % 256 == 0 (the reference also needs M % 128 == 0).
+ * SFA/SFB must span blackhole_sm100_sf_storage_bytes(M|N, K) bytes (rows padded to 128).
+ * Pointers must be 16-byte aligned.  Errors: cudaErrorInvalidValue for a bad shape,
+ * null or misaligned pointer; otherwise the launch status, as in nvfp4_gemm.hpp:594-636. */
+BLACKHOLE_SM100_API int blackhole_sm100_nvfp4_bf16_gemm(int M, int N, int K, const void* A, const void* SFA,
+                                    const void* B, const void* SFB, void* D, float alpha,
+                                    cudaStream_t stream);
+
+/* Bytes of a (mn x k) scale-factor tensor in the 128x4 layout, padding included
+ * (the cosize of make_layout_SFA/SFB; nvfp4_gemm.hpp:293-302). */
+BLACKHOLE_SM100_API int64_t blackhole_sm100_sf_storage_bytes(int64_t mn, int64_t k);
+
+/* Byte offset of the scale factor of row mn, K-group kg (= k/16) for K extent k
+ * (make_layout_SFA(M, K)(mn, kg*16); nvfp4_gemm.hpp:293-298). */
+BLACKHOLE_SM100_API int64_t blackhole_sm100_sf_offset(int64_t mn, int64_t kg, int64_t k);
+
+/* Device-side status of the calling process's kernels on `device`: nonzero when a kernel
+ * gave up on a bounded wait (bit 0: load pipeline, bit 1: MMA pipeline, bit 2: epilogue).
+ * Synchronises the device.  With clear != 0 the word is reset afterwards.  The reference
+ * has no counterpart (its kernel cannot time out). */
+BLACKHOLE_SM100_API int blackhole_sm100_device_status(int device, unsigned int* status, int clear);
+
+/* NVFP4 quantiser: X (rows x K, FP32 when x_is_bf16 == 0, else BF16, K-contiguous,
+ * K % 16 == 0) -> packed E2M1 (rows*K/2 bytes), UE4M3 scale factors in the 128x4 layout
+ * (sf_storage_bytes(rows, K) bytes, padding written as 0) and scales[0] = amax,
+ * scales[1] = global scale g = amax/(448*6) (device float[2]).  Per 16-block:
+ * s = UE4M3((amax_b/6)/g), q = E2M1(x/(s*g)), all round-to-nearest-even; alpha of a GEMM
+ * is gA*gB.  Device counterpart of the reference example's host quantisation
+ * (example/nvfp4_bf16_gemm.cu:60-71, :104-133), following the BASELINE recipe. */
+BLACKHOLE_SM100_API int blackhole_sm100_nvfp4_quantize(const void* X, int x_is_bf16, int rows, int K,
+                                                       void* packed, void* sf, float* scales,
+                                                       cudaStream_t stream);
+
+/* ABI version of the loaded library (BLACKHOLE_SM100_ABI_VERSION). */
+BLACKHOLE_SM100_API int blackhole_sm100_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BLACKHOLE_SM100_H */

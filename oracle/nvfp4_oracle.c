@@ -265,11 +265,42 @@ static void run_jobs(gemm_job* base, int64_t total, int nthreads) {
   for (int t = 0; t < nthreads; ++t) pthread_join(tid[t], NULL);
 }
 
+typedef struct {
+  const uint8_t *P, *SF;
+  int64_t K, r0, r1;
+  float* out;
+} dequant_job;
+
+static void* dequant_worker(void* arg) {
+  dequant_job* j = (dequant_job*)arg;
+  for (int64_t r = j->r0; r < j->r1; ++r) dequant_row(j->P, j->SF, r, j->K, j->out + r * j->K);
+  return NULL;
+}
+
+static void dequant_rows_parallel(const uint8_t* P, const uint8_t* SF, int64_t rows, int64_t K,
+                                  float* out, int nthreads) {
+  if (nthreads < 1) nthreads = 1;
+  if (nthreads > 256) nthreads = 256;
+  if (nthreads > rows) nthreads = (int)(rows > 0 ? rows : 1);
+  pthread_t tid[256];
+  dequant_job jobs[256];
+  for (int t = 0; t < nthreads; ++t) {
+    dequant_job j = {P, SF, K, rows * t / nthreads, rows * (t + 1) / nthreads, out};
+    jobs[t] = j;
+  }
+  if (nthreads == 1) {
+    dequant_worker(&jobs[0]);
+    return;
+  }
+  for (int t = 0; t < nthreads; ++t) pthread_create(&tid[t], NULL, dequant_worker, &jobs[t]);
+  for (int t = 0; t < nthreads; ++t) pthread_join(tid[t], NULL);
+}
+
 void bho_gemm_ref_full(int64_t M, int64_t N, int64_t K, const uint8_t* A, const uint8_t* SFA,
                        const uint8_t* B, const uint8_t* SFB, float alpha, uint16_t* D,
                        double* absdot, int nthreads) {
   float* Bdq = (float*)malloc(sizeof(float) * (size_t)(N * K));
-  for (int64_t n = 0; n < N; ++n) dequant_row(B, SFB, n, K, Bdq + n * K);
+  dequant_rows_parallel(B, SFB, N, K, Bdq, nthreads);
   gemm_job job = {M, N, K, A, SFA, B, SFB, alpha, D, absdot, Bdq, 0, 0, 0, NULL, NULL, 0};
   run_jobs(&job, M, nthreads);
   free(Bdq);

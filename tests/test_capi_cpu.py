@@ -1,0 +1,65 @@
+"""C-ABI host checks that need no GPU: the library loads, exports every symbol that
+include/*.h declares, agrees with the oracle on the scale-factor layout, and rejects bad
+arguments with cudaErrorInvalidValue before any device work."""
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+import blackhole_b200 as bh
+from oracle import oracle as O
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    syms = set()
+    inc = os.path.join(ROOT, "include")
+    for f in os.listdir(inc):
+        if f.endswith(".h"):
+            src = open(os.path.join(inc, f)).read()
+            syms |= set(re.findall(r"BLACKHOLE_SM100_API\s+[\w\s\*]+?\b(blackhole_\w+)\s*\(", src))
+    return syms
+
+
+def test_library_exports_every_declared_symbol():
+    syms = declared_symbols()
+    assert "blackhole_sm100_nvfp4_bf16_gemm" in syms and len(syms) >= 5
+    out = subprocess.run(["nm", "-D", "--defined-only", bh.LIB_PATH], capture_output=True, text=True).stdout
+    exported = {l.split()[-1] for l in out.splitlines() if " T " in l}
+    missing = syms - exported
+    assert not missing, f"declared but not exported: {missing}"
+    L = bh.load()
+    for s in syms:
+        assert hasattr(L, s)
+    assert L.blackhole_sm100_abi_version() == 1
+
+
+@pytest.mark.parametrize("mn,k", [(1, 256), (16, 8192), (200, 768), (28672, 8192), (8192, 8192)])
+def test_sf_layout_matches_oracle(mn, k):
+    assert bh.sf_storage_bytes(mn, k) == O.sf_storage_bytes(mn, k)
+    for m in (0, 1, 31, 32, 127, 128, mn - 1):
+        if m >= mn:
+            continue
+        for kg in (0, 1, 3, 4, k // 16 - 1):
+            assert bh.sf_offset(m, kg, k) == O.sf_offset(m, kg, k)
+
+
+@pytest.mark.parametrize("M,N,K", [(0, 128, 256), (128, 0, 256), (128, 100, 256), (128, 128, 128),
+                                   (128, 128, 320), (-1, 128, 256), (128, 64, 256)])
+def test_bad_shapes_rejected_before_launch(M, N, K):
+    with pytest.raises(bh.BlackholeError) as ei:
+        bh.nvfp4_bf16_gemm(M, N, K, 4096, 4096, 4096, 4096, 4096, 1.0, stream=0)
+    assert ei.value.code == 1  # cudaErrorInvalidValue
+
+
+def test_null_and_misaligned_pointers_rejected():
+    good = 1 << 20
+    for args in [(0, good, good, good, good), (good, 0, good, good, good), (good, good, good, good, 0),
+                 (good + 8, good, good, good, good), (good, good, good + 4, good, good),
+                 (good, good, good, good, good + 2)]:
+        with pytest.raises(bh.BlackholeError) as ei:
+            bh.nvfp4_bf16_gemm(128, 128, 256, *args, 1.0, stream=0)
+        assert ei.value.code == 1
