@@ -39,8 +39,8 @@ FALLBACK_BF16_TFLOPS = 1590.0
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=400)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=8192, help="columns per GPU")
@@ -76,7 +76,7 @@ class ClockSampler:
     REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
                "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, device_index, interval=0.02):
+    def __init__(self, device_index, interval=0.005):
         self.samples, self.reasons = [], set()
         self.max_mhz = None
         self._stop = threading.Event()

@@ -16,6 +16,7 @@ import os
 __all__ = [
     "LIB_PATH", "load", "nvfp4_bf16_gemm", "sf_storage_bytes", "sf_offset",
     "device_status", "BlackholeError", "nvfp4_quantize", "quantize_tensor",
+    "nvfp4_bf16_gemm_ex", "workspace_bytes", "SCHEDULES",
 ]
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -49,6 +50,11 @@ def load():
     vp, i32, i64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
     L.blackhole_sm100_nvfp4_bf16_gemm.restype = i32
     L.blackhole_sm100_nvfp4_bf16_gemm.argtypes = [i32, i32, i32, vp, vp, vp, vp, vp, ctypes.c_float, vp]
+    L.blackhole_sm100_nvfp4_bf16_gemm_ex.restype = i32
+    L.blackhole_sm100_nvfp4_bf16_gemm_ex.argtypes = [i32, i32, i32, vp, vp, vp, vp, vp, ctypes.c_float,
+                                                     i32, vp, i64, vp]
+    L.blackhole_sm100_workspace_bytes.restype = i64
+    L.blackhole_sm100_workspace_bytes.argtypes = [i32, i32, i32]
     L.blackhole_sm100_sf_storage_bytes.restype = i64
     L.blackhole_sm100_sf_storage_bytes.argtypes = [i64, i64]
     L.blackhole_sm100_sf_offset.restype = i64
@@ -103,6 +109,32 @@ def nvfp4_bf16_gemm(M: int, N: int, K: int, A, SFA, B, SFB, D, alpha: float = 1.
         float(alpha), _stream(stream))
     if rc != 0:
         raise BlackholeError("blackhole_sm100_nvfp4_bf16_gemm", rc)
+
+
+SCHEDULES = {"auto": 0, "1sm": 1, "2sm": 2, "skinny": 3}
+
+
+def nvfp4_bf16_gemm_ex(M: int, N: int, K: int, A, SFA, B, SFB, D, alpha: float = 1.0,
+                       schedule: str = "auto", workspace=None, workspace_bytes: int = 0,
+                       stream=None) -> None:
+    """nvfp4_bf16_gemm with an explicit schedule ("auto", "1sm", "2sm", "skinny") and an
+    optional caller-owned workspace for the skinny schedule (see workspace_bytes)."""
+    if workspace is not None and hasattr(workspace, "numel") and not workspace_bytes:
+        workspace_bytes = workspace.numel() * workspace.element_size()
+    rc = load().blackhole_sm100_nvfp4_bf16_gemm_ex(
+        int(M), int(N), int(K), _ptr(A), _ptr(SFA), _ptr(B), _ptr(SFB), _ptr(D), float(alpha),
+        SCHEDULES[schedule], _ptr(workspace) if workspace is not None else None,
+        int(workspace_bytes), _stream(stream))
+    if rc != 0:
+        raise BlackholeError("blackhole_sm100_nvfp4_bf16_gemm_ex", rc)
+
+
+def workspace_bytes(M: int, N: int, K: int) -> int:
+    """Workspace bytes the skinny schedule needs on the current device (0 if unused)."""
+    v = int(load().blackhole_sm100_workspace_bytes(int(M), int(N), int(K)))
+    if v < 0:
+        raise BlackholeError("blackhole_sm100_workspace_bytes", 1)
+    return v
 
 
 def sf_storage_bytes(mn: int, k: int) -> int:

@@ -3,7 +3,7 @@
 // =====================================================================================
 // blackhole / sm100 / NVFP4 (E2M1 + UE4M3 per-16 block scale) x NVFP4 -> BF16 GEMM
 // -------------------------------------------------------------------------------------
-// D = bf16(alpha * A . B^T) on B200 (sm_100a), written directly in PTX:
+// D = bf16(alpha * A . B^T) on B200 (sm_100a), hand-written tcgen05 / TMA PTX:
 //
 //   * A: M x K E2M1, K-contiguous, two values per byte (even k in the low nibble)
 //   * B: N x K E2M1, K-contiguous
@@ -14,24 +14,17 @@
 // Same operator call as the reference's sm_120 kernel
 // (include/blackhole/sm120/nvfp4_gemm.hpp:588-637), plus an alpha (global scale) overload.
 //
-// Kernel structure (one persistent CTA per SM, 10 warps):
+// Schedules (chosen by shape):
+//   * M <= 128 : skinny schedule (nvfp4_gemm_skinny.hpp) -- swap-AB, stream-K over all SMs,
+//                HBM-bound; needs a small FP32 workspace (allocated here per device and
+//                stream on first use, or passed by the caller: nvfp4_bf16_gemm_ws);
+//   * M > 128  : two-SM schedule (nvfp4_gemm_2sm.hpp) -- 256 x 256 tiles per CTA pair,
+//                tensor-bound;
+//   * the one-SM schedule (nvfp4_gemm_1sm.hpp, 128 x 256 tiles) is available explicitly.
 //
-//   warp 0 (TMA)   : for each k-tile of 256 K: TMA 128x128B of A and 256x128B of B
-//                    (128B swizzle) and bulk-copy the 2 KB + 4 KB scale-factor atoms into a
-//                    4-stage shared-memory ring; full/empty mbarrier pair per stage.
-//   warp 1 (MMA)   : tcgen05.cp the scale factors smem -> TMEM, then four
-//                    tcgen05.mma.kind::mxf4nvf4.block_scale (128x256x64 each) per k-tile
-//                    into a 128 x 256 FP32 accumulator in TMEM; tcgen05.commit frees the
-//                    smem stage; after the last k-tile it signals the epilogue.
-//   warps 2-9 (epi): tcgen05.ld the accumulator (two warps per 32-lane sub-partition, 128
-//                    columns each), release TMEM to the MMA warp at once, then alpha * acc
-//                    -> BF16 -> global while the next tile's mainloop runs.
-//
-// Every mbarrier wait is bounded; a stalled pipeline records a status bit (readable through
-// blackhole_sm100_device_status) and the kernel returns.
-//
-// Shapes: M >= 1 (TMA zero-fills rows past M; stores are masked), N % 128 == 0,
-// K % 256 == 0.  The reference additionally requires M % 128 == 0 (nvfp4_gemm.hpp:594).
+// Shapes: M >= 1, N % 128 == 0, K % 256 == 0.  The reference additionally requires
+// M % 128 == 0 (nvfp4_gemm.hpp:594).  Every mbarrier wait in the kernels is bounded: a
+// stalled pipeline records a status bit (blackhole_sm100_device_status) and returns.
 // =====================================================================================
 
 #include <cstddef>
@@ -43,427 +36,93 @@
 #include <blackhole/common/sf_layout.hpp>
 #include <blackhole_sm100.h>
 
+#include <blackhole/sm100/nvfp4_gemm_common.hpp>
+
 #if defined(__CUDACC__)
-#include <cuda.h>
-#include <cuda_bf16.h>
-#include <cuda_runtime.h>
+#include <map>
+#include <utility>
 
-#include <mutex>
-
-#include <blackhole/sm100/ptx.hpp>
+#include <blackhole/sm100/nvfp4_gemm_1sm.hpp>
+#include <blackhole/sm100/nvfp4_gemm_2sm.hpp>
+#include <blackhole/sm100/nvfp4_gemm_skinny.hpp>
 #endif
 
 namespace blackhole::sm100 {
 
-// =====================================================================================
-// 1. Compile-time configuration
-// =====================================================================================
-struct Nvfp4GemmTraits {
-  static constexpr int SFVecSize = kNvfp4SfVec;  // 16 elements per scale factor
-
-  static constexpr int TileM = 128;              // UMMA M (one CTA, TMEM lanes)
-  static constexpr int TileN = 256;              // UMMA N
-  static constexpr int TileK = 256;              // elements per k-tile = one 128 B row
-  static constexpr int MmaK = 64;                // elements per tcgen05.mma (32 bytes)
-  static constexpr int KSteps = TileK / MmaK;    // 4 MMAs per k-tile
-  static constexpr int Stages = 4;
-
-  static constexpr int RowBytes = TileK / 2;                        // 128
-  static constexpr int ABytes = TileM * RowBytes;                   // 16 KB
-  static constexpr int BBytes = TileN * RowBytes;                   // 32 KB
-  static constexpr int SFABytes = (TileM / 128) * KSteps * 512;     // 2 KB
-  static constexpr int SFBBytes = (TileN / 128) * KSteps * 512;     // 4 KB
-  static constexpr int StageBytes = ABytes + BBytes + SFABytes + SFBBytes;
-
-  static constexpr int NumWarps = 10;
-  static constexpr int NumThreads = NumWarps * 32;
-  static constexpr int ProducerWarp = 0;
-  static constexpr int MmaWarp = 1;
-  static constexpr int FirstEpiWarp = 2;
-  static constexpr int NumEpiWarps = 8;
-
-  // TMEM columns: accumulator [0,256), SFA 4 per k-step, SFB 8 per k-step.
-  static constexpr uint32_t TmemCols = 512;
-  static constexpr uint32_t AccCol = 0;
-  static constexpr uint32_t SfaCol = 256;
-  static constexpr uint32_t SfbCol = SfaCol + 4 * KSteps;
-
-  // shared memory: stage ring + barriers (+1 KB to align the ring to 1024 B)
-  static constexpr int BarrierBytes = 8 * (2 * Stages + 4) + 16;
-  static constexpr int SmemBytes = Stages * StageBytes + BarrierBytes + 1024;
-
-  static constexpr int RasterGroupM = 16;  // tiles walk 16 M-blocks at a time (L2 reuse)
-
-  static_assert(SmemBytes <= arch_traits<Arch::kSm100>::max_smem_per_cta, "smem budget");
-  static_assert(SfbCol + 8 * KSteps <= TmemCols, "TMEM budget");
-};
-
-// Status bits written when a bounded wait gives up.
-enum : uint32_t {
-  kStatusLoadTimeout = 1u,
-  kStatusMmaTimeout = 2u,
-  kStatusEpilogueTimeout = 4u,
-};
-
-// Shape / alignment check shared by the launcher and the C ABI.
-inline cudaError_t nvfp4_check_args(int M, int N, int K, const void* A, const void* SFA,
-                                    const void* B, const void* SFB, const void* D) {
-  if (M < 1 || N < 128 || K < 256) return cudaErrorInvalidValue;
-  if (N % 128 != 0 || K % 256 != 0) return cudaErrorInvalidValue;
-  if (!A || !SFA || !B || !SFB || !D) return cudaErrorInvalidValue;
-  auto mis = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) != 0; };
-  if (mis(A) || mis(SFA) || mis(B) || mis(SFB) || mis(D)) return cudaErrorInvalidValue;
-  // TMA: row pitch K/2 bytes < 2^40, 32-bit coordinates; tile counts fit in int.
-  if (static_cast<int64_t>(M) * N > (int64_t(1) << 46)) return cudaErrorInvalidValue;
-  return cudaSuccess;
-}
+enum class Nvfp4Schedule : int { kAuto = 0, kOneSm = 1, kTwoSm = 2, kSkinny = 3 };
 
 #if defined(__CUDACC__)
 
-// =====================================================================================
-// 2. Kernel
-// =====================================================================================
-struct Nvfp4GemmParams {
-  CUtensorMap tmap_a;   // A as uint8 [M][K/2], box 128 x 128 B, 128B swizzle
-  CUtensorMap tmap_b;   // B as uint8 [N][K/2], box 256 x 128 B, 128B swizzle
-  const uint8_t* sfa;
-  const uint8_t* sfb;
-  uint16_t* d;
-  uint32_t* status;
-  float alpha;
-  int M, N, K;
-  int tiles_m, tiles_n, num_tiles;
-  int k_tiles;
-  int sf_k_atoms;       // 512-byte SF atoms along K per 128-row block
-  int n_blocks128;      // N / 128
-};
-
 namespace detail {
 
-template <class KT>
-__device__ __forceinline__ void tile_coords(int tile, const Nvfp4GemmParams& p, int& m_blk,
-                                            int& n_blk) {
-  const int group_tiles = KT::RasterGroupM * p.tiles_n;
-  const int group = tile / group_tiles;
-  const int first_m = group * KT::RasterGroupM;
-  const int rows = min(KT::RasterGroupM, p.tiles_m - first_m);
-  const int local = tile - group * group_tiles;
-  m_blk = first_m + local % rows;
-  n_blk = local / rows;
-}
-
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&v);
-}
-
-// Bounded wait used only on the abort path: does not look at the abort flag.
-__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
-  const uint64_t t0 = ptx::globaltimer_ns();
-  while (!ptx::mbar_try_wait(bar, parity)) {
-    if (ptx::globaltimer_ns() - t0 > 200000000ull) break;
-  }
-}
-
-}  // namespace detail
-
-template <class KT>
-__global__ void __launch_bounds__(KT::NumThreads, 1)
-    nvfp4_gemm_kernel(const __grid_constant__ Nvfp4GemmParams p) {
-#if defined(BLACKHOLE_ARCH_SM100)
-  using namespace ptx;
-  constexpr int S = KT::Stages;
-
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t raw = smem_u32(smem_raw);
-  const uint32_t base = (raw + 1023u) & ~1023u;
-  uint8_t* const base_ptr = smem_raw + (base - raw);
-
-  const uint32_t sA = base;
-  const uint32_t sB = sA + S * KT::ABytes;
-  const uint32_t sSFA = sB + S * KT::BBytes;
-  const uint32_t sSFB = sSFA + S * KT::SFABytes;
-  const uint32_t bars = sSFB + S * KT::SFBBytes;
-  auto full_bar = [&](int s) { return bars + 8u * s; };
-  auto empty_bar = [&](int s) { return bars + 8u * (S + s); };
-  const uint32_t acc_full = bars + 16u * S;
-  const uint32_t acc_empty = acc_full + 8u;
-  const uint32_t drain_bar = acc_full + 16u;
-  uint32_t* const tmem_slot = reinterpret_cast<uint32_t*>(base_ptr + (bars - base) + 16 * S + 32);
-  volatile int* const abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(full_bar(s), 1);
-      mbar_init(empty_bar(s), 1);
-    }
-    mbar_init(acc_full, 1);
-    mbar_init(acc_empty, KT::NumEpiWarps);
-    mbar_init(drain_bar, 1);
-    *abort_flag = 0;
-    fence_mbar_init();
-    fence_proxy_async_smem();
-  }
-  if (warp == KT::MmaWarp) {
-    tmem_alloc(smem_u32(tmem_slot), KT::TmemCols);
-    tmem_relinquish();
-  }
-  if (warp == KT::ProducerWarp && lane == 0) {
-    prefetch_tmap(&p.tmap_a);
-    prefetch_tmap(&p.tmap_b);
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == KT::ProducerWarp) {
-    // ------------------------------ TMA producer ------------------------------------
-    if (lane == 0) {
-      const uint64_t pol_a = l2_policy_evict_last();
-      const uint64_t pol_b = l2_policy_evict_last();
-      int stage = 0;
-      uint32_t phase = 0;
-      int64_t issued = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
-        int m_blk, n_blk;
-        detail::tile_coords<KT>(tile, p, m_blk, n_blk);
-        const bool sfb_hi = (2 * n_blk + 1) < p.n_blocks128;
-        const uint32_t bytes =
-            KT::ABytes + KT::BBytes + KT::SFABytes + (sfb_hi ? KT::SFBBytes : KT::SFBBytes / 2);
-        const uint8_t* sfa_src = p.sfa + (int64_t(m_blk) * p.sf_k_atoms) * 512;
-        const uint8_t* sfb_src0 = p.sfb + (int64_t(2 * n_blk) * p.sf_k_atoms) * 512;
-        const uint8_t* sfb_src1 = sfb_src0 + int64_t(p.sf_k_atoms) * 512;
-        for (int kt = 0; kt < p.k_tiles; ++kt) {
-          if (!wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, p.status,
-                            kStatusLoadTimeout)) {
-            ok = false;
-            break;
-          }
-          const uint32_t fb = full_bar(stage);
-          mbar_arrive_expect_tx(fb, bytes);
-          tma_load_2d(sA + stage * KT::ABytes, &p.tmap_a, fb, kt * KT::RowBytes, m_blk * KT::TileM,
-                      pol_a);
-          tma_load_2d(sB + stage * KT::BBytes, &p.tmap_b, fb, kt * KT::RowBytes, n_blk * KT::TileN,
-                      pol_b);
-          const int64_t k_off = int64_t(kt) * KT::KSteps * 512;
-          bulk_load(sSFA + stage * KT::SFABytes, sfa_src + k_off, KT::SFABytes, fb, pol_a);
-          bulk_load(sSFB + stage * KT::SFBBytes, sfb_src0 + k_off, KT::SFBBytes / 2, fb, pol_b);
-          if (sfb_hi)
-            bulk_load(sSFB + stage * KT::SFBBytes + KT::SFBBytes / 2, sfb_src1 + k_off,
-                      KT::SFBBytes / 2, fb, pol_b);
-          ++issued;
-          if (++stage == S) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
-      }
-      if (!ok) {
-        // Let the copies already in flight land before the CTA goes away.
-        for (int s = 0; s < S; ++s) {
-          if (issued > s) {
-            const int64_t cnt = (issued - 1 - s) / S + 1;
-            detail::drain_wait(full_bar(s), uint32_t((cnt - 1) & 1));
-          }
-        }
-      }
-    }
-  } else if (warp == KT::MmaWarp) {
-    // ------------------------------ MMA issuer --------------------------------------
-    constexpr uint32_t idesc = idesc_nvf4(KT::TileM, KT::TileN);
-    int stage = 0;
-    uint32_t phase = 0;
-    uint32_t acc_phase = 0;
-    bool ok = true;
-    bool issued_any = false;
-    for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
-      if (!wait_bounded(acc_empty, acc_phase ^ 1u, abort_flag, p.status, kStatusMmaTimeout)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      for (int kt = 0; kt < p.k_tiles; ++kt) {
-        if (!wait_bounded(full_bar(stage), phase, abort_flag, p.status, kStatusMmaTimeout)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        if (lane == 0) {
-          const uint32_t sfa_s = sSFA + stage * KT::SFABytes;
-          const uint32_t sfb_s = sSFB + stage * KT::SFBBytes;
-#pragma unroll
-          for (int j = 0; j < KT::KSteps; ++j) {
-            tc_cp_32x128b_warpx4(tmem + KT::SfaCol + 4 * j, desc_sf_atom(sfa_s + 512 * j));
-            tc_cp_32x128b_warpx4(tmem + KT::SfbCol + 8 * j, desc_sf_atom(sfb_s + 512 * j));
-            tc_cp_32x128b_warpx4(tmem + KT::SfbCol + 8 * j + 4,
-                                 desc_sf_atom(sfb_s + KT::SFBBytes / 2 + 512 * j));
-          }
-          const uint64_t adesc = desc_kmajor_sw128(sA + stage * KT::ABytes);
-          const uint64_t bdesc = desc_kmajor_sw128(sB + stage * KT::BBytes);
-#pragma unroll
-          for (int j = 0; j < KT::KSteps; ++j) {
-            // +32 bytes of K per step inside the 128-byte swizzle row (descriptor units: 16 B)
-            tc_mma_nvf4(tmem + KT::AccCol, adesc + 2 * j, bdesc + 2 * j, idesc,
-                        tmem + KT::SfaCol + 4 * j, tmem + KT::SfbCol + 8 * j,
-                        (kt | j) != 0 ? 1u : 0u);
-          }
-          tc_commit(empty_bar(stage));
-          issued_any = true;
-        }
-        __syncwarp();
-        if (++stage == S) {
-          stage = 0;
-          phase ^= 1u;
-        }
-      }
-      if (!ok) break;
-      if (lane == 0) tc_commit(acc_full);
-      __syncwarp();
-      acc_phase ^= 1u;
-    }
-    if (!ok && lane == 0 && issued_any) {
-      // wait for the MMAs in flight before TMEM is released
-      tc_commit(drain_bar);
-      detail::drain_wait(drain_bar, 0);
-    }
-    __syncwarp();
-  } else {
-    // ------------------------------ epilogue ----------------------------------------
-    const int q = warp & 3;                                   // TMEM lane quadrant
-    const int half = (warp - KT::FirstEpiWarp) >> 2;          // column half of the tile
-    const uint32_t t_row = tmem + (static_cast<uint32_t>(32 * q) << 16) + KT::AccCol + 128 * half;
-    uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
-      int m_blk, n_blk;
-      detail::tile_coords<KT>(tile, p, m_blk, n_blk);
-      if (!wait_bounded(acc_full, acc_phase, abort_flag, p.status, kStatusEpilogueTimeout)) break;
-      tc_fence_after();
-      uint32_t v0[32], v1[32], v2[32], v3[32];
-      tmem_ld_32x32b_x32(t_row + 0, v0);
-      tmem_ld_32x32b_x32(t_row + 32, v1);
-      tmem_ld_32x32b_x32(t_row + 64, v2);
-      tmem_ld_32x32b_x32(t_row + 96, v3);
-      tmem_ld_wait();
-      reg_fence(v0);
-      reg_fence(v1);
-      reg_fence(v2);
-      reg_fence(v3);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty);
-      acc_phase ^= 1u;
-
-      const int row = m_blk * KT::TileM + 32 * q + lane;
-      const int col0 = n_blk * KT::TileN + 128 * half;
-      if (row < p.M && col0 < p.N) {
-        uint16_t* dst = p.d + static_cast<int64_t>(row) * p.N + col0;
-        const float a = p.alpha;
-        auto emit = [&](uint32_t (&v)[32], int c) {
-#pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            st_global_v4(dst + c + i,
-                         detail::pack_bf16x2(a * __uint_as_float(v[i + 0]), a * __uint_as_float(v[i + 1])),
-                         detail::pack_bf16x2(a * __uint_as_float(v[i + 2]), a * __uint_as_float(v[i + 3])),
-                         detail::pack_bf16x2(a * __uint_as_float(v[i + 4]), a * __uint_as_float(v[i + 5])),
-                         detail::pack_bf16x2(a * __uint_as_float(v[i + 6]), a * __uint_as_float(v[i + 7])));
-          }
-        };
-        emit(v0, 0);
-        emit(v1, 32);
-        emit(v2, 64);
-        emit(v3, 96);
-      }
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == KT::MmaWarp) {
-    tc_fence_after();
-    tmem_dealloc(tmem, KT::TmemCols);
-  }
-#endif  // BLACKHOLE_ARCH_SM100
-}
-
-// =====================================================================================
-// 3. Host launcher
-// =====================================================================================
-namespace detail {
-
-static __device__ uint32_t g_status;  // or-ed status bits of this module's kernels
-
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-inline EncodeTiledFn encode_tiled_fn() {
-  static EncodeTiledFn fn = []() -> EncodeTiledFn {
+// Workspace of the skinny schedule owned by the library: one per (device, stream), grown
+// on demand, flag words zeroed at allocation.  Calls on the same stream are ordered, so
+// they may share it; different streams get different buffers.
+inline cudaError_t library_workspace(int dev, cudaStream_t stream, int64_t bytes, void** out) {
+  struct Ws {
     void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) !=
-            cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      return nullptr;
-    return reinterpret_cast<EncodeTiledFn>(ptr);
-  }();
-  return fn;
-}
-
-// 2-D K-major byte tensor [rows][row_bytes] with a (box_rows x 128 B) box, 128B swizzle.
-inline cudaError_t make_kmajor_tmap(CUtensorMap* m, const void* base, int64_t rows,
-                                    int64_t row_bytes, uint32_t box_rows) {
-  EncodeTiledFn enc = encode_tiled_fn();
-  if (!enc) return cudaErrorNotSupported;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
-  cuuint32_t box[2] = {128u, box_rows};
-  cuuint32_t estr[2] = {1u, 1u};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
-                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
-}
-
-struct DeviceState {
-  std::once_flag once;
-  cudaError_t init_err = cudaSuccess;
-  int num_sms = 0;
-  uint32_t* status = nullptr;
-};
-
-inline DeviceState& device_state(int dev) {
-  static DeviceState states[64];
-  return states[dev & 63];
-}
-
-// Per-device one-time set-up (the reference keeps a process-wide static bool instead,
-// nvfp4_gemm.hpp:625-631, which misses every device after the first).
-template <class KT>
-inline DeviceState* prepare_device() {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  DeviceState& st = device_state(dev);
-  std::call_once(st.once, [&]() {
-    st.init_err = cudaFuncSetAttribute(nvfp4_gemm_kernel<KT>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, KT::SmemBytes);
-    if (st.init_err != cudaSuccess) return;
-    st.init_err = cudaDeviceGetAttribute(&st.num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (st.init_err != cudaSuccess) return;
-    void* sym = nullptr;
-    st.init_err = cudaGetSymbolAddress(&sym, g_status);
-    st.status = static_cast<uint32_t*>(sym);
-  });
-  return &st;
+    int64_t bytes = 0;
+  };
+  static std::mutex mu;
+  static std::map<std::pair<int, uintptr_t>, Ws> pool;
+  std::lock_guard<std::mutex> lock(mu);
+  Ws& w = pool[{dev, reinterpret_cast<uintptr_t>(stream)}];
+  if (w.bytes < bytes) {
+    if (w.ptr) {
+      cudaError_t e = cudaStreamSynchronize(stream);
+      if (e != cudaSuccess) return e;
+      cudaFree(w.ptr);
+      w.ptr = nullptr;
+      w.bytes = 0;
+    }
+    cudaError_t e = cudaMalloc(&w.ptr, static_cast<size_t>(bytes));
+    if (e != cudaSuccess) return e;
+    e = cudaMemset(w.ptr, 0, static_cast<size_t>(bytes));
+    if (e != cudaSuccess) return e;
+    w.bytes = bytes;
+  }
+  *out = w.ptr;
+  return cudaSuccess;
 }
 
 }  // namespace detail
+
+// Full control: schedule choice and (for the skinny schedule) a caller-owned workspace.
+// workspace == nullptr selects the library-owned workspace.
+inline cudaError_t nvfp4_bf16_gemm_ex(int M, int N, int K, void const* A, void const* SFA,
+                                      void const* B, void const* SFB, void* D, float alpha,
+                                      Nvfp4Schedule schedule, void* workspace,
+                                      int64_t workspace_bytes, cudaStream_t stream) {
+  cudaError_t e = nvfp4_check_args(M, N, K, A, SFA, B, SFB, D);
+  if (e != cudaSuccess) return e;
+  detail::DeviceState* st = detail::prepare_device();
+  if (!st) return cudaErrorInvalidDevice;
+  if (st->init_err != cudaSuccess) return st->init_err;
+  int dev = 0;
+  e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (schedule == Nvfp4Schedule::kAuto)
+    schedule = M <= 128 ? Nvfp4Schedule::kSkinny : Nvfp4Schedule::kTwoSm;
+  switch (schedule) {
+    case Nvfp4Schedule::kOneSm:
+      return detail::launch_1sm<Nvfp4GemmTraits>(M, N, K, A, SFA, B, SFB, D, alpha, st, dev, stream);
+    case Nvfp4Schedule::kTwoSm:
+      return detail::launch_2sm<Nvfp4Gemm2SmTraits>(M, N, K, A, SFA, B, SFB, D, alpha, st, dev, stream);
+    case Nvfp4Schedule::kSkinny: {
+      if (M > 128) return cudaErrorInvalidValue;
+      const int64_t need = nvfp4_skinny_workspace_bytes(st->num_sms, nvfp4_skinny_mpad(M));
+      if (!workspace) {
+        e = detail::library_workspace(dev, stream, need, &workspace);
+        if (e != cudaSuccess) return e;
+        workspace_bytes = need;
+      }
+      return nvfp4_bf16_gemm_skinny(M, N, K, A, SFA, B, SFB, D, alpha, workspace, workspace_bytes,
+                                    stream);
+    }
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
 
 //   A_packed : E2M1, M x K, K-contiguous (two per byte, low nibble first)
 //   SFA      : UE4M3 in the 128x4 layout (make_layout_SFA(M, K)), sf_storage_bytes(M, K) bytes
@@ -473,36 +132,8 @@ inline DeviceState* prepare_device() {
 inline cudaError_t nvfp4_bf16_gemm(int M, int N, int K, void const* A_packed, void const* SFA,
                                    void const* B_packed, void const* SFB, void* D, float alpha,
                                    cudaStream_t stream = nullptr) {
-  using KT = Nvfp4GemmTraits;
-  cudaError_t e = nvfp4_check_args(M, N, K, A_packed, SFA, B_packed, SFB, D);
-  if (e != cudaSuccess) return e;
-  detail::DeviceState* st = detail::prepare_device<KT>();
-  if (!st) return cudaErrorInvalidDevice;
-  if (st->init_err != cudaSuccess) return st->init_err;
-
-  Nvfp4GemmParams p;
-  e = detail::make_kmajor_tmap(&p.tmap_a, A_packed, M, K / 2, KT::TileM);
-  if (e != cudaSuccess) return e;
-  e = detail::make_kmajor_tmap(&p.tmap_b, B_packed, N, K / 2, KT::TileN);
-  if (e != cudaSuccess) return e;
-  p.sfa = static_cast<const uint8_t*>(SFA);
-  p.sfb = static_cast<const uint8_t*>(SFB);
-  p.d = static_cast<uint16_t*>(D);
-  p.status = st->status;
-  p.alpha = alpha;
-  p.M = M;
-  p.N = N;
-  p.K = K;
-  p.tiles_m = (M + KT::TileM - 1) / KT::TileM;
-  p.tiles_n = (N + KT::TileN - 1) / KT::TileN;
-  p.num_tiles = p.tiles_m * p.tiles_n;
-  p.k_tiles = K / KT::TileK;
-  p.sf_k_atoms = static_cast<int>(sf_k_atoms(K));
-  p.n_blocks128 = N / 128;
-
-  const int grid = p.num_tiles < st->num_sms ? p.num_tiles : st->num_sms;
-  nvfp4_gemm_kernel<KT><<<grid, KT::NumThreads, KT::SmemBytes, stream>>>(p);
-  return cudaGetLastError();
+  return nvfp4_bf16_gemm_ex(M, N, K, A_packed, SFA, B_packed, SFB, D, alpha, Nvfp4Schedule::kAuto,
+                            nullptr, 0, stream);
 }
 
 // The reference's exact nine-argument call (alpha = 1).
@@ -510,22 +141,6 @@ inline cudaError_t nvfp4_bf16_gemm(int M, int N, int K, void const* A_packed, vo
                                    void const* B_packed, void const* SFB, void* D,
                                    cudaStream_t stream = nullptr) {
   return nvfp4_bf16_gemm(M, N, K, A_packed, SFA, B_packed, SFB, D, 1.0f, stream);
-}
-
-// Reads (and optionally clears) the status word of this module on the current device.
-inline cudaError_t read_device_status(unsigned int* out, bool clear) {
-  detail::DeviceState* st = detail::prepare_device<Nvfp4GemmTraits>();
-  if (!st) return cudaErrorInvalidDevice;
-  if (st->init_err != cudaSuccess) return st->init_err;
-  cudaError_t e = cudaDeviceSynchronize();
-  if (e != cudaSuccess) return e;
-  e = cudaMemcpyFromSymbol(out, detail::g_status, sizeof(unsigned int));
-  if (e != cudaSuccess) return e;
-  if (clear) {
-    unsigned int z = 0;
-    e = cudaMemcpyToSymbol(detail::g_status, &z, sizeof(unsigned int));
-  }
-  return e;
 }
 
 #else  // !__CUDACC__: host-compiler users reach the same operator through the C ABI.
@@ -543,8 +158,5 @@ inline cudaError_t nvfp4_bf16_gemm(int M, int N, int K, void const* A_packed, vo
 }
 
 #endif  // __CUDACC__
-
-// Host layout helpers with the reference's names (nvfp4_gemm.hpp:293-302).
-inline int64_t sf_storage_bytes_for(int MN, int K) { return blackhole::sf_storage_bytes(MN, K); }
 
 }  // namespace blackhole::sm100

@@ -1,0 +1,405 @@
+#pragma once
+
+// =====================================================================================
+// blackhole / sm100 / NVFP4 GEMM, two-SM schedule (cta_group::2, 256 x 256 tiles)
+// -------------------------------------------------------------------------------------
+// A cluster of two CTAs (one TPC) computes a 256 x 256 output tile with
+// tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 64 per instruction):
+//
+//   * CTA r of the pair loads rows [128r, 128r+128) of the A tile and of the B tile, its
+//     own 128 rows of SFA and all 256 rows of SFB (TMA, 128B swizzle for A/B) into a
+//     5-stage ring of 38 KB stages.  Every load of either CTA completes on the leader CTA's
+//     "full" barrier (TMA .cta_group::2), which expects the bytes of both CTAs.
+//   * The leader's MMA warp copies both CTAs' scale factors to their TMEM
+//     (tcgen05.cp.cta_group::2) and issues the MMAs, which read A/B halves from both CTAs'
+//     shared memory and write each CTA's 128 x 256 FP32 accumulator into its own TMEM.
+//     Its commits arrive on the "empty" barriers of both CTAs and, per tile, on both CTAs'
+//     "acc_full" barriers.
+//   * Each CTA's 8 epilogue warps drain its own accumulator, arrive on the leader's
+//     "acc_empty" barrier and write alpha * acc as BF16 through a 128B-swizzled 4 KB
+//     shared-memory box per warp and a TMA tensor store (full-line, coalesced writes; the
+//     store clips rows / columns past the edge of D).
+//
+// Per SM and per 128-clock MMA this moves 38 KB into shared memory instead of the 54 KB a
+// one-SM 128 x 256 tile needs, and B crosses L2 -> SM once per pair instead of twice.
+// Scale factors are fetched through tensor maps so ragged M / N edges read zeros.
+// =====================================================================================
+
+#include <blackhole/sm100/nvfp4_gemm_common.hpp>
+
+namespace blackhole::sm100 {
+
+template <int TileK_ = 256, int Stages_ = 5>
+struct Nvfp4Gemm2SmTraitsT {
+  static constexpr int TileM = 256;              // per pair (UMMA M)
+  static constexpr int CtaM = 128;
+  static constexpr int TileN = 256;              // UMMA N
+  static constexpr int CtaN = 128;               // B rows held per CTA
+  static constexpr int TileK = TileK_;
+  static constexpr int KSteps = TileK / 64;
+  static constexpr int Stages = Stages_;
+
+  static constexpr int RowBytes = TileK / 2;
+  static constexpr int ABytes = CtaM * RowBytes;           // 16 KB
+  static constexpr int BBytes = CtaN * RowBytes;           // 16 KB
+  static constexpr int SFABytes = KSteps * 512;            // 2 KB (own 128 rows)
+  static constexpr int SFBBytes = 2 * KSteps * 512;        // 4 KB (all 256 rows)
+  static constexpr int StageBytes = ABytes + BBytes + SFABytes + SFBBytes;
+
+  static constexpr int NumWarps = 10;
+  static constexpr int NumThreads = NumWarps * 32;
+  static constexpr int ProducerWarp = 0;
+  static constexpr int MmaWarp = 1;
+  static constexpr int FirstEpiWarp = 2;
+  static constexpr int NumEpiWarps = 8;
+
+  static constexpr uint32_t TmemCols = 512;
+  static constexpr uint32_t AccCol = 0;
+  static constexpr uint32_t SfaCol = 256;
+  static constexpr uint32_t SfbCol = SfaCol + 4 * KSteps;
+
+  // epilogue staging: one 32-row x 64-column BF16 box (4 KB, 128B-swizzled) per epilogue warp
+  static constexpr int StoreBoxBytes = 32 * 64 * 2;
+  static constexpr int StagingBytes = NumEpiWarps * StoreBoxBytes;
+
+  static constexpr int BarrierBytes = 8 * (2 * Stages + 4) + 16;
+  static constexpr int SmemBytes = Stages * StageBytes + StagingBytes + BarrierBytes + 1024;
+  static constexpr int RasterGroupM = 8;         // in 256-row tiles
+
+  static_assert(SmemBytes <= arch_traits<Arch::kSm100>::max_smem_per_cta, "smem budget");
+};
+using Nvfp4Gemm2SmTraits = Nvfp4Gemm2SmTraitsT<256, 5>;
+
+#if defined(__CUDACC__)
+
+struct Nvfp4Gemm2SmParams {
+  CUtensorMap tmap_a;     // A  [M][K/2] bytes, box 128 x 128 B, 128B swizzle
+  CUtensorMap tmap_b;     // B  [N][K/2] bytes, box 128 x 128 B, 128B swizzle
+  CUtensorMap tmap_sfa;   // SFA atoms [M/128 * K/64][512 B], box 4 atoms
+  CUtensorMap tmap_sfb;   // SFB atoms [N/128 * K/64][512 B], box 4 atoms
+  CUtensorMap tmap_d;     // D  [M][N] bf16, box 32 rows x 64 columns, 128B swizzle
+  uint32_t* status;
+  float alpha;
+  int M, N, K;
+  int tiles_m, tiles_n, num_tiles;
+  int k_tiles;
+  int sf_k_atoms;
+};
+
+namespace detail {
+
+__device__ __forceinline__ void tile_coords_2sm(int tile, const Nvfp4Gemm2SmParams& p, int& m_blk,
+                                                int& n_blk) {
+  constexpr int G = 8;  // raster group, in 256-row tiles
+  const int group_tiles = G * p.tiles_n;
+  const int group = tile / group_tiles;
+  const int first_m = group * G;
+  const int rows = min(G, p.tiles_m - first_m);
+  const int local = tile - group * group_tiles;
+  m_blk = first_m + local % rows;
+  n_blk = local / rows;
+}
+
+}  // namespace detail
+
+template <class KT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
+    nvfp4_gemm_2sm_kernel(const __grid_constant__ Nvfp4Gemm2SmParams p) {
+#if defined(BLACKHOLE_ARCH_SM100)
+  using namespace ptx;
+  constexpr int S = KT::Stages;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* const base_ptr = smem_raw + (base - raw);
+
+  const uint32_t sA = base;
+  const uint32_t sB = sA + S * KT::ABytes;
+  const uint32_t sSFA = sB + S * KT::BBytes;
+  const uint32_t sSFB = sSFA + S * KT::SFABytes;
+  const uint32_t sStage = sSFB + S * KT::SFBBytes;   // epilogue staging boxes
+  const uint32_t bars = sStage + KT::StagingBytes;
+  auto full_bar = [&](int s) { return bars + 8u * s; };
+  auto empty_bar = [&](int s) { return bars + 8u * (S + s); };
+  const uint32_t acc_full = bars + 16u * S;
+  const uint32_t acc_empty = acc_full + 8u;
+  const uint32_t drain_bar = acc_full + 16u;
+  uint32_t* const tmem_slot = reinterpret_cast<uint32_t*>(base_ptr + (bars - base) + 16 * S + 32);
+  volatile int* const abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();          // 0 = leader, 1 = peer
+  const int cluster = blockIdx.x >> 1;
+  const int num_clusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 2 * KT::NumEpiWarps);
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == KT::MmaWarp) {
+    tmem_alloc_pair(smem_u32(tmem_slot), KT::TmemCols);
+    tmem_relinquish_pair();
+  }
+  if (warp == KT::ProducerWarp && lane == 0) {
+    prefetch_tmap(&p.tmap_a);
+    prefetch_tmap(&p.tmap_b);
+    prefetch_tmap(&p.tmap_sfa);
+    prefetch_tmap(&p.tmap_sfb);
+    prefetch_tmap(&p.tmap_d);
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // barriers of both CTAs initialised before any cross-CTA signal
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == KT::ProducerWarp) {
+    // ------------------------------ TMA producer (both CTAs) ------------------------
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      int64_t issued = 0;
+      bool ok = true;
+      for (int tile = cluster; ok && tile < p.num_tiles; tile += num_clusters) {
+        int m_blk, n_blk;
+        detail::tile_coords_2sm(tile, p, m_blk, n_blk);
+        const int a_row = m_blk * KT::TileM + int(rank) * KT::CtaM;
+        const int b_row = n_blk * KT::TileN + int(rank) * KT::CtaN;
+        const int sfa_atom = (m_blk * 2 + int(rank)) * p.sf_k_atoms;
+        const int sfb_atom0 = (n_blk * 2) * p.sf_k_atoms;
+        const int sfb_atom1 = sfb_atom0 + p.sf_k_atoms;
+        for (int kt = 0; kt < p.k_tiles; ++kt) {
+          if (!wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, p.status, kStatusLoadTimeout)) {
+            ok = false;
+            break;
+          }
+          const uint32_t lb = mapa_shared(full_bar(stage), 0);
+          if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), 2u * KT::StageBytes);
+          tma_load_2d_pair(sA + stage * KT::ABytes, &p.tmap_a, lb, kt * KT::RowBytes, a_row, pol);
+          tma_load_2d_pair(sB + stage * KT::BBytes, &p.tmap_b, lb, kt * KT::RowBytes, b_row, pol);
+          tma_load_2d_pair(sSFA + stage * KT::SFABytes, &p.tmap_sfa, lb, 0, sfa_atom + KT::KSteps * kt, pol);
+          tma_load_2d_pair(sSFB + stage * KT::SFBBytes, &p.tmap_sfb, lb, 0, sfb_atom0 + KT::KSteps * kt, pol);
+          tma_load_2d_pair(sSFB + stage * KT::SFBBytes + KT::SFBBytes / 2, &p.tmap_sfb, lb, 0,
+                           sfb_atom1 + KT::KSteps * kt, pol);
+          ++issued;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok && rank == 0) {
+        for (int s = 0; s < S; ++s) {
+          if (issued > s) {
+            const int64_t cnt = (issued - 1 - s) / S + 1;
+            detail::drain_wait(full_bar(s), uint32_t((cnt - 1) & 1));
+          }
+        }
+      }
+    }
+  } else if (warp == KT::MmaWarp) {
+    // ------------------------------ MMA issuer (leader CTA) -------------------------
+    if (rank == 0) {
+      constexpr uint32_t idesc = idesc_nvf4(KT::TileM, KT::TileN);
+      const uint32_t acc_full_0 = mapa_shared(acc_full, 0);
+      const uint32_t acc_full_1 = mapa_shared(acc_full, 1);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      bool issued_any = false;
+      for (int tile = cluster; ok && tile < p.num_tiles; tile += num_clusters) {
+        if (!wait_bounded_warp(acc_empty, acc_phase ^ 1u, abort_flag, p.status, kStatusMmaTimeout)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int kt = 0; kt < p.k_tiles; ++kt) {
+          if (!wait_bounded_warp(full_bar(stage), phase, abort_flag, p.status, kStatusMmaTimeout)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          {
+            const uint32_t sfa_s = sSFA + stage * KT::SFABytes;
+            const uint32_t sfb_s = sSFB + stage * KT::SFBBytes;
+#pragma unroll
+            for (int j = 0; j < KT::KSteps; ++j) {
+              tc_cp_32x128b_warpx4_pair_w(tmem + KT::SfaCol + 4 * j, desc_sf_atom(sfa_s + 512 * j));
+              tc_cp_32x128b_warpx4_pair_w(tmem + KT::SfbCol + 8 * j, desc_sf_atom(sfb_s + 512 * j));
+              tc_cp_32x128b_warpx4_pair_w(tmem + KT::SfbCol + 8 * j + 4,
+                                          desc_sf_atom(sfb_s + KT::SFBBytes / 2 + 512 * j));
+            }
+            const uint64_t adesc = desc_kmajor<KT::RowBytes>(sA + stage * KT::ABytes);
+            const uint64_t bdesc = desc_kmajor<KT::RowBytes>(sB + stage * KT::BBytes);
+#pragma unroll
+            for (int j = 0; j < KT::KSteps; ++j) {
+              tc_mma_nvf4_pair_w(tmem + KT::AccCol, adesc + 2 * j, bdesc + 2 * j, idesc,
+                                 tmem + KT::SfaCol + 4 * j, tmem + KT::SfbCol + 8 * j,
+                                 (kt | j) != 0 ? 1u : 0u);
+            }
+            tc_commit_pair_w(mapa_shared(empty_bar(stage), 0));
+            tc_commit_pair_w(mapa_shared(empty_bar(stage), 1));
+            issued_any = true;
+          }
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair_w(acc_full_0);
+        tc_commit_pair_w(acc_full_1);
+        acc_phase ^= 1u;
+      }
+      if (!ok && issued_any) {
+        tc_commit_pair_w(mapa_shared(drain_bar, 0));
+        detail::drain_wait(drain_bar, 0);
+      }
+      __syncwarp();
+    }
+  } else {
+    // ------------------------------ epilogue (both CTAs) ----------------------------
+    const int q = warp & 3;
+    const int half = (warp - KT::FirstEpiWarp) >> 2;
+    const uint32_t t_row = tmem + (static_cast<uint32_t>(32 * q) << 16) + KT::AccCol + 128 * half;
+    const uint32_t leader_acc_empty = mapa_shared(acc_empty, 0);
+    uint32_t acc_phase = 0;
+    for (int tile = cluster; tile < p.num_tiles; tile += num_clusters) {
+      int m_blk, n_blk;
+      detail::tile_coords_2sm(tile, p, m_blk, n_blk);
+      if (!wait_bounded_warp(acc_full, acc_phase, abort_flag, p.status, kStatusEpilogueTimeout)) break;
+      tc_fence_after();
+      uint32_t v0[32], v1[32], v2[32], v3[32];
+      tmem_ld_32x32b_x32(t_row + 0, v0);
+      tmem_ld_32x32b_x32(t_row + 32, v1);
+      tmem_ld_32x32b_x32(t_row + 64, v2);
+      tmem_ld_32x32b_x32(t_row + 96, v3);
+      tmem_ld_wait();
+      reg_fence(v0);
+      reg_fence(v1);
+      reg_fence(v2);
+      reg_fence(v3);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(leader_acc_empty);
+      acc_phase ^= 1u;
+
+      // alpha * acc -> BF16 -> this warp's swizzled staging box -> TMA store, 64 columns at
+      // a time.  Lane i owns row i of the box; its 16-byte chunk c lands at chunk c ^ (i % 8)
+      // of the 128-byte row, the layout CU_TENSOR_MAP_SWIZZLE_128B expects.
+      const int row0 = m_blk * KT::TileM + int(rank) * KT::CtaM + 32 * q;
+      const int col0 = n_blk * KT::TileN + 128 * half;
+      const uint32_t box = sStage + (warp - KT::FirstEpiWarp) * KT::StoreBoxBytes;
+      const uint32_t my_row = box + lane * 128;
+      const float a = p.alpha;
+      auto stage_store = [&](uint32_t (&va)[32], uint32_t (&vb)[32], int u) {
+        if (lane == 0) bulk_wait_group_read<0>();   // previous box has been read out
+        __syncwarp();
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint32_t (&v)[32] = c < 4 ? va : vb;
+          const int i = (c & 3) * 8;
+          st_shared_v4(my_row + ((c ^ (lane & 7)) << 4),
+                       detail::pack_bf16x2(a * __uint_as_float(v[i + 0]), a * __uint_as_float(v[i + 1])),
+                       detail::pack_bf16x2(a * __uint_as_float(v[i + 2]), a * __uint_as_float(v[i + 3])),
+                       detail::pack_bf16x2(a * __uint_as_float(v[i + 4]), a * __uint_as_float(v[i + 5])),
+                       detail::pack_bf16x2(a * __uint_as_float(v[i + 6]), a * __uint_as_float(v[i + 7])));
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && row0 < p.M && col0 + 64 * u < p.N) {
+          tma_store_2d(&p.tmap_d, box, col0 + 64 * u, row0);
+          bulk_commit_group();
+        }
+      };
+      stage_store(v0, v1, 0);
+      stage_store(v2, v3, 1);
+    }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its partner may still signal it
+  if (warp == KT::MmaWarp) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, KT::TmemCols);
+  }
+#endif  // BLACKHOLE_ARCH_SM100
+}
+
+namespace detail {
+
+template <class KT>
+inline cudaError_t launch_2sm(int M, int N, int K, const void* A, const void* SFA, const void* B,
+                              const void* SFB, void* D, float alpha, DeviceState* st, int dev,
+                              cudaStream_t stream) {
+  cudaError_t e = set_smem_once(nvfp4_gemm_2sm_kernel<KT>, KT::SmemBytes, dev);
+  if (e != cudaSuccess) return e;
+  Nvfp4Gemm2SmParams p;
+  e = make_kmajor_tmap(&p.tmap_a, A, M, K / 2, KT::CtaM, KT::RowBytes);
+  if (e != cudaSuccess) return e;
+  e = make_kmajor_tmap(&p.tmap_b, B, N, K / 2, KT::CtaN, KT::RowBytes);
+  if (e != cudaSuccess) return e;
+  e = make_sf_tmap(&p.tmap_sfa, SFA, M, K, KT::KSteps);
+  if (e != cudaSuccess) return e;
+  e = make_sf_tmap(&p.tmap_sfb, SFB, N, K, KT::KSteps);
+  if (e != cudaSuccess) return e;
+  e = make_d_tmap(&p.tmap_d, D, M, N);
+  if (e != cudaSuccess) return e;
+  p.status = st->status;
+  p.alpha = alpha;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.tiles_m = (M + KT::TileM - 1) / KT::TileM;
+  p.tiles_n = (N + KT::TileN - 1) / KT::TileN;
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  p.k_tiles = K / KT::TileK;
+  p.sf_k_atoms = static_cast<int>(sf_k_atoms(K));
+  // Persistent grid = the number of 2-CTA clusters that can be resident at once.  GPCs with
+  // an odd number of usable SMs leave an SM idle, so this is below num_sms / 2; launching
+  // num_sms / 2 clusters would run the excess as a second wave.
+  static std::mutex mu;
+  static int resident[64] = {0};
+  int clusters = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (resident[dev & 63] == 0) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(static_cast<unsigned>(st->num_sms & ~1), 1, 1);
+      cfg.blockDim = dim3(KT::NumThreads, 1, 1);
+      cfg.dynamicSmemBytes = KT::SmemBytes;
+      int n = 0;
+      e = cudaOccupancyMaxActiveClusters(&n, nvfp4_gemm_2sm_kernel<KT>, &cfg);
+      if (e != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = st->num_sms / 2;
+      }
+      resident[dev & 63] = n;
+    }
+    clusters = resident[dev & 63];
+  }
+  if (p.num_tiles < clusters) clusters = p.num_tiles;
+  nvfp4_gemm_2sm_kernel<KT><<<2 * clusters, KT::NumThreads, KT::SmemBytes, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace detail
+
+#endif  // __CUDACC__
+
+}  // namespace blackhole::sm100

@@ -1,0 +1,202 @@
+#pragma once
+
+// Shared host/device pieces of the sm_100a NVFP4 GEMM schedules: argument checks, status
+// word, tensor-map encoding and per-device state.
+
+#include <cstddef>
+#include <cstdint>
+
+#include <cuda_runtime_api.h>
+
+#include <blackhole/common/arch.hpp>
+#include <blackhole/common/sf_layout.hpp>
+
+#if defined(__CUDACC__)
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <map>
+#include <mutex>
+#include <utility>
+
+#include <blackhole/sm100/ptx.hpp>
+#endif
+
+namespace blackhole::sm100 {
+
+// Status bits written when a bounded wait gives up.
+enum : uint32_t {
+  kStatusLoadTimeout = 1u,
+  kStatusMmaTimeout = 2u,
+  kStatusEpilogueTimeout = 4u,
+};
+
+// Shape / alignment check shared by every schedule and the C ABI (host only, no CUDA calls).
+// The reference accepts M % 128 == 0, N % 128 == 0, K % 256 == 0 (nvfp4_gemm.hpp:594-596);
+// here any M >= 1 is accepted.
+inline cudaError_t nvfp4_check_args(int M, int N, int K, const void* A, const void* SFA,
+                                    const void* B, const void* SFB, const void* D) {
+  if (M < 1 || N < 128 || K < 256) return cudaErrorInvalidValue;
+  if (N % 128 != 0 || K % 256 != 0) return cudaErrorInvalidValue;
+  if (!A || !SFA || !B || !SFB || !D) return cudaErrorInvalidValue;
+  auto mis = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) != 0; };
+  if (mis(A) || mis(SFA) || mis(B) || mis(SFB) || mis(D)) return cudaErrorInvalidValue;
+  if (static_cast<int64_t>(M) * N > (int64_t(1) << 46)) return cudaErrorInvalidValue;
+  return cudaSuccess;
+}
+
+#if defined(__CUDACC__)
+
+namespace detail {
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Bounded wait used only on the abort path: does not look at the abort flag.
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = ptx::globaltimer_ns();
+  while (!ptx::mbar_try_wait(bar, parity)) {
+    if (ptx::globaltimer_ns() - t0 > 200000000ull) break;
+  }
+}
+
+static __device__ uint32_t g_status;  // or-ed status bits of this module's kernels
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline EncodeTiledFn encode_tiled_fn() {
+  static EncodeTiledFn fn = []() -> EncodeTiledFn {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<EncodeTiledFn>(ptr);
+  }();
+  return fn;
+}
+
+// 2-D K-major byte tensor [rows][row_bytes] with a (box_rows x box_bytes) box swizzled at
+// box_bytes (128, 64 or 32).  Rows past `rows` read as zero.
+inline cudaError_t make_kmajor_tmap(CUtensorMap* m, const void* base, int64_t rows,
+                                    int64_t row_bytes, uint32_t box_rows, uint32_t box_bytes = 128) {
+  EncodeTiledFn enc = encode_tiled_fn();
+  if (!enc) return cudaErrorNotSupported;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+  cuuint32_t box[2] = {box_bytes, box_rows};
+  cuuint32_t estr[2] = {1u, 1u};
+  const CUtensorMapSwizzle swz = box_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                 : box_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                   : CU_TENSOR_MAP_SWIZZLE_32B;
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+// Scale factors viewed as rows of 512-byte atoms (64 x 8 bytes): [row_blocks * k_atoms][64].
+// A box of box_atoms atoms is one (64 * box_atoms)-wide k-tile of one 128-row block; atoms
+// past the end (row blocks beyond the tensor) read as zero.
+inline cudaError_t make_sf_tmap(CUtensorMap* m, const void* base, int64_t mn, int64_t k,
+                                uint32_t box_atoms = 4) {
+  EncodeTiledFn enc = encode_tiled_fn();
+  if (!enc) return cudaErrorNotSupported;
+  const int64_t atoms = ((mn + 127) / 128) * sf_k_atoms(k);
+  cuuint64_t dims[2] = {64u, static_cast<cuuint64_t>(atoms)};
+  cuuint64_t strides[1] = {512u};
+  cuuint32_t box[2] = {64u, box_atoms};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+// Row-major BF16 [rows][cols] output with a (32 rows x 64 columns) box, 128B swizzle: the
+// store box of one epilogue warp.  Parts of a box past the tensor edge are not written.
+inline cudaError_t make_d_tmap(CUtensorMap* m, void* base, int64_t rows, int64_t cols) {
+  EncodeTiledFn enc = encode_tiled_fn();
+  if (!enc) return cudaErrorNotSupported;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * 2)};
+  cuuint32_t box[2] = {64u, 32u};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+struct DeviceState {
+  std::once_flag once;
+  cudaError_t init_err = cudaSuccess;
+  int num_sms = 0;
+  uint32_t* status = nullptr;
+};
+
+inline DeviceState& device_state(int dev) {
+  static DeviceState states[64];
+  return states[dev & 63];
+}
+
+// Per-device one-time set-up (the reference keeps a process-wide static bool instead,
+// nvfp4_gemm.hpp:625-631, which misses every device after the first).
+inline DeviceState* prepare_device() {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  DeviceState& st = device_state(dev);
+  std::call_once(st.once, [&]() {
+    st.init_err = cudaDeviceGetAttribute(&st.num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (st.init_err != cudaSuccess) return;
+    void* sym = nullptr;
+    st.init_err = cudaGetSymbolAddress(&sym, g_status);
+    st.status = static_cast<uint32_t*>(sym);
+  });
+  return &st;
+}
+
+// Sets a kernel's dynamic shared-memory limit once per (device, kernel function).
+template <class Kernel>
+inline cudaError_t set_smem_once(Kernel kernel, int bytes, int dev) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, cudaError_t> done;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_pair(dev, reinterpret_cast<const void*>(kernel));
+  auto it = done.find(key);
+  if (it != done.end()) return it->second;
+  const cudaError_t e =
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  done[key] = e;
+  return e;
+}
+
+}  // namespace detail
+
+// Reads (and optionally clears) the status word of this module on the current device.
+inline cudaError_t read_device_status(unsigned int* out, bool clear) {
+  detail::DeviceState* st = detail::prepare_device();
+  if (!st) return cudaErrorInvalidDevice;
+  if (st->init_err != cudaSuccess) return st->init_err;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return e;
+  e = cudaMemcpyFromSymbol(out, detail::g_status, sizeof(unsigned int));
+  if (e != cudaSuccess) return e;
+  if (clear) {
+    unsigned int z = 0;
+    e = cudaMemcpyToSymbol(detail::g_status, &z, sizeof(unsigned int));
+  }
+  return e;
+}
+
+#endif  // __CUDACC__
+
+}  // namespace blackhole::sm100

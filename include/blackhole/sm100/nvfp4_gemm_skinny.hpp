@@ -1,0 +1,479 @@
+#pragma once
+
+// =====================================================================================
+// blackhole / sm100 / NVFP4 GEMM, skinny-M schedule (M <= 128: decode-style shapes)
+// -------------------------------------------------------------------------------------
+// For M <= 128 the GEMM is bound by streaming B (N x K/2 bytes + its scale factors) from
+// HBM.  This schedule computes D^T = B . A^T so that 128 rows of B fill the UMMA M = 128
+// and the M activation rows become the UMMA N (padded to MPAD = 16/32/64/128; TMA
+// zero-fills rows >= M):
+//
+//   * work unit = (128-row block rb of B, 256-wide k-tile kt); U = N/128 * K/256 units are
+//     split into equal contiguous ranges, one per persistent CTA (stream-K), so every SM
+//     streams the same number of bytes;
+//   * each CTA walks its range backwards in row-block segments; a segment accumulates in
+//     one of two TMEM accumulators (128 lanes x MPAD FP32 columns) so its epilogue overlaps
+//     the next segment's loads and MMAs;
+//   * a row block that spans several CTAs is finished by the CTA owning its last k-tile:
+//     the others (which reach it first) park FP32 partials in the workspace and raise a
+//     flag per epilogue warp; the finisher's matching warp adds them in a fixed order
+//     (deterministic) and writes BF16.  Only warps exchange data, never whole CTAs, so no
+//     CTA-wide barrier sits in the epilogue.
+//
+// Each CTA parks at most one partial, so the workspace is 4 flags per CTA plus
+// grid * MPAD * 128 * 4 bytes of partials (nvfp4_skinny_workspace_bytes).
+// Flags are raised to 1 by the producer of a partial and reset to 0 by its consumer, so a
+// workspace is reusable by later launches on the same stream (and by graph replays).
+// Because finishers wait only on lower-numbered CTAs, which were launched no later, the
+// dependency never points at a CTA that cannot be resident.
+// =====================================================================================
+
+#include <cstdint>
+
+#include <blackhole/sm100/nvfp4_gemm_common.hpp>
+
+namespace blackhole::sm100 {
+
+template <int MPAD_>
+struct Nvfp4SkinnyTraits {
+  static constexpr int MPAD = MPAD_;            // UMMA N
+  static constexpr int TileW = 128;             // rows of B per unit (UMMA M)
+  static constexpr int TileK = 256;
+  static constexpr int KSteps = 4;
+  static constexpr int RowBytes = 128;
+  static constexpr int WBytes = TileW * RowBytes;           // 16 KB
+  static constexpr int XBytes = MPAD * RowBytes;            // 2..16 KB
+  static constexpr int SFBytes = KSteps * 512;              // 2 KB per operand
+  static constexpr int StageBytes = WBytes + XBytes + 2 * SFBytes;
+  static constexpr int Stages = (MPAD <= 32) ? 9 : (MPAD == 64 ? 8 : 6);
+
+  static constexpr int NumWarps = 6;                        // TMA, MMA, 4 x epilogue
+  static constexpr int NumThreads = NumWarps * 32;
+  static constexpr int ProducerWarp = 0;
+  static constexpr int MmaWarp = 1;
+  static constexpr int FirstEpiWarp = 2;
+
+  static constexpr uint32_t TmemCols = 512;
+  static constexpr uint32_t AccStride = 128;                // two accumulators: [0,128), [128,256)
+  static constexpr uint32_t SfwCol = 256;                   // 4 columns per k-step
+  static constexpr uint32_t SfxCol = 256 + 4 * KSteps;      // 4 columns per k-step
+
+  static constexpr int BarrierBytes = 8 * (2 * Stages + 5) + 16;
+  static constexpr int SmemBytes = Stages * StageBytes + BarrierBytes + 1024;
+  static_assert(SmemBytes <= arch_traits<Arch::kSm100>::max_smem_per_cta, "smem budget");
+  static_assert(MPAD % 16 == 0 && MPAD >= 16 && MPAD <= 128, "UMMA N");
+};
+
+// Workspace layout: flag words first, at a fixed place for the device (4 per possible CTA,
+// padded to 256 bytes), then the FP32 partials.  Keeping the flags at a fixed offset means a
+// workspace shared by calls of different M never sees partial data where a flag should be.
+inline int64_t nvfp4_skinny_flag_bytes(int num_sms) {
+  return (int64_t(num_sms) * 16 + 255) / 256 * 256;
+}
+// Bytes of workspace the skinny schedule needs on a device with num_sms SMs at width mpad.
+inline int64_t nvfp4_skinny_workspace_bytes(int num_sms, int mpad) {
+  return nvfp4_skinny_flag_bytes(num_sms) + int64_t(num_sms) * mpad * 128 * 4;
+}
+
+inline int nvfp4_skinny_mpad(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128; }
+
+#if defined(__CUDACC__)
+
+struct Nvfp4SkinnyParams {
+  CUtensorMap tmap_w;   // B [N][K/2] bytes, box 128 rows x 128 B
+  CUtensorMap tmap_x;   // A [M][K/2] bytes, box MPAD rows x 128 B
+  const uint8_t* sfw;   // SFB
+  const uint8_t* sfx;   // SFA
+  uint16_t* d;
+  float* ws;            // [grid][MPAD][128] partials
+  uint32_t* flags;      // [grid][4]: one per epilogue warp
+  uint32_t* status;
+  float alpha;
+  int M, N, K;
+  int kt_per_rb;        // K / 256
+  int64_t units;        // N/128 * K/256
+  int grid;
+  int sf_k_atoms;
+};
+
+namespace skinny_detail {
+
+__device__ __forceinline__ int64_t range_start(const Nvfp4SkinnyParams& p, int c) {
+  return int64_t(c) * p.units / p.grid;
+}
+
+// One row-block segment of a CTA's range, visited from the end of the range backwards.
+struct Segment {
+  int rb, kt0, kt1;
+};
+
+struct SegmentWalk {
+  int64_t begin, u;
+  int KT;
+  __device__ __forceinline__ bool next(Segment& s) {
+    if (u <= begin) return false;
+    const int rb = static_cast<int>((u - 1) / KT);
+    const int64_t rb0 = int64_t(rb) * KT;
+    const int64_t sb = begin > rb0 ? begin : rb0;
+    s.rb = rb;
+    s.kt0 = static_cast<int>(sb - rb0);
+    s.kt1 = static_cast<int>(u - rb0);
+    u = sb;
+    return true;
+  }
+};
+
+__device__ __forceinline__ SegmentWalk walk(const Nvfp4SkinnyParams& p, int c) {
+  SegmentWalk w;
+  w.begin = range_start(p, c);
+  w.u = range_start(p, c + 1);
+  w.KT = p.kt_per_rb;
+  return w;
+}
+
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+}  // namespace skinny_detail
+
+template <class KT>
+__global__ void __launch_bounds__(KT::NumThreads, 1)
+    nvfp4_gemm_skinny_kernel(const __grid_constant__ Nvfp4SkinnyParams p) {
+#if defined(BLACKHOLE_ARCH_SM100)
+  using namespace ptx;
+  using namespace skinny_detail;
+  constexpr int S = KT::Stages;
+  constexpr int MPAD = KT::MPAD;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* const base_ptr = smem_raw + (base - raw);
+  auto st_w = [&](int s) { return base + uint32_t(s) * KT::StageBytes; };
+  auto st_x = [&](int s) { return st_w(s) + KT::WBytes; };
+  auto st_sfw = [&](int s) { return st_x(s) + KT::XBytes; };
+  auto st_sfx = [&](int s) { return st_sfw(s) + KT::SFBytes; };
+  const uint32_t bars = base + S * KT::StageBytes;
+  auto full_bar = [&](int s) { return bars + 8u * s; };
+  auto empty_bar = [&](int s) { return bars + 8u * (S + s); };
+  auto acc_full = [&](int a) { return bars + 8u * (2 * S + a); };
+  auto acc_empty = [&](int a) { return bars + 8u * (2 * S + 2 + a); };
+  const uint32_t drain_bar = bars + 8u * (2 * S + 4);
+  uint32_t* const tmem_slot =
+      reinterpret_cast<uint32_t*>(base_ptr + (bars - base) + 8 * (2 * S + 5));
+  volatile int* const abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int c = blockIdx.x;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(acc_full(a), 1);
+      mbar_init(acc_empty(a), 4);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == KT::MmaWarp) {
+    tmem_alloc(smem_u32(tmem_slot), KT::TmemCols);
+    tmem_relinquish();
+  }
+  if (warp == KT::ProducerWarp && lane == 0) {
+    prefetch_tmap(&p.tmap_w);
+    prefetch_tmap(&p.tmap_x);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == KT::ProducerWarp) {
+    // ------------------------------ TMA producer ------------------------------------
+    if (lane == 0) {
+      const uint64_t pol_w = l2_policy_evict_first();   // B is streamed exactly once
+      const uint64_t pol_x = l2_policy_evict_last();    // A is re-read by every CTA
+      int stage = 0;
+      uint32_t phase = 0;
+      int64_t issued = 0;
+      bool ok = true;
+      SegmentWalk w = walk(p, c);
+      Segment sg;
+      while (ok && w.next(sg)) {
+        const uint8_t* sfw_rb = p.sfw + int64_t(sg.rb) * p.sf_k_atoms * 512;
+        for (int kt = sg.kt0; kt < sg.kt1; ++kt) {
+          if (!wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, p.status, kStatusLoadTimeout)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = full_bar(stage);
+          mbar_arrive_expect_tx(fb, KT::StageBytes);
+          tma_load_2d(st_w(stage), &p.tmap_w, fb, kt * KT::RowBytes, sg.rb * KT::TileW, pol_w);
+          tma_load_2d(st_x(stage), &p.tmap_x, fb, kt * KT::RowBytes, 0, pol_x);
+          const int64_t k_off = int64_t(kt) * KT::KSteps * 512;
+          bulk_load(st_sfw(stage), sfw_rb + k_off, KT::SFBytes, fb, pol_w);
+          bulk_load(st_sfx(stage), p.sfx + k_off, KT::SFBytes, fb, pol_x);
+          ++issued;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        for (int s = 0; s < S; ++s) {
+          if (issued > s) {
+            const int64_t cnt = (issued - 1 - s) / S + 1;
+            detail::drain_wait(full_bar(s), uint32_t((cnt - 1) & 1));
+          }
+        }
+      }
+    }
+  } else if (warp == KT::MmaWarp) {
+    // ------------------------------ MMA issuer --------------------------------------
+    constexpr uint32_t idesc = idesc_nvf4(128, MPAD);
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true, issued_any = false;
+    SegmentWalk w = walk(p, c);
+    Segment sg;
+    while (ok && w.next(sg)) {
+      if (!wait_bounded_warp(acc_empty(acc), acc_phase ^ 1u, abort_flag, p.status, kStatusMmaTimeout)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem + KT::AccStride * acc;
+      for (int kt = sg.kt0; kt < sg.kt1; ++kt) {
+        if (!wait_bounded_warp(full_bar(stage), phase, abort_flag, p.status, kStatusMmaTimeout)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        {
+#pragma unroll
+          for (int j = 0; j < KT::KSteps; ++j) {
+            tc_cp_32x128b_warpx4_w(tmem + KT::SfwCol + 4 * j, desc_sf_atom(st_sfw(stage) + 512 * j));
+            tc_cp_32x128b_warpx4_w(tmem + KT::SfxCol + 4 * j, desc_sf_atom(st_sfx(stage) + 512 * j));
+          }
+          const uint64_t wdesc = desc_kmajor_sw128(st_w(stage));
+          const uint64_t xdesc = desc_kmajor_sw128(st_x(stage));
+#pragma unroll
+          for (int j = 0; j < KT::KSteps; ++j) {
+            tc_mma_nvf4_w(d_tmem, wdesc + 2 * j, xdesc + 2 * j, idesc, tmem + KT::SfwCol + 4 * j,
+                          tmem + KT::SfxCol + 4 * j, (kt != sg.kt0 || j != 0) ? 1u : 0u);
+          }
+          tc_commit_w(empty_bar(stage));
+          issued_any = true;
+        }
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      tc_commit_w(acc_full(acc));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if (!ok && issued_any) {
+      tc_commit_w(drain_bar);
+      detail::drain_wait(drain_bar, 0);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------ epilogue ----------------------------------------
+    const int q = warp & 3;
+    const int n_local = 32 * q + lane;                            // row of the B block
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    SegmentWalk w = walk(p, c);
+    Segment sg;
+    while (w.next(sg)) {
+      if (!wait_bounded_warp(acc_full(acc), acc_phase, abort_flag, p.status, kStatusEpilogueTimeout))
+        break;
+      tc_fence_after();
+      float v[MPAD];
+      {
+        const uint32_t t = tmem + (static_cast<uint32_t>(32 * q) << 16) + KT::AccStride * acc;
+#pragma unroll
+        for (int j = 0; j < MPAD / 16; ++j) {
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(t + 16 * j, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            asm volatile("" : "+r"(r[i]));
+            v[16 * j + i] = __uint_as_float(r[i]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty(acc));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+
+      const int n = sg.rb * 128 + n_local;
+      if (sg.kt1 != p.kt_per_rb) {
+        // Partial of a row block finished by a later CTA: park it, then raise this warp's flag.
+        float* dst = p.ws + (int64_t(c) * MPAD) * 128 + n_local;
+#pragma unroll
+        for (int m = 0; m < MPAD; ++m)
+          if (m < p.M) __stcg(dst + m * 128, v[m]);
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) st_release(p.flags + 4 * c + q, 1u);
+        continue;
+      }
+      if (sg.kt0 > 0) {
+        // Finisher: add the partials of the earlier CTAs that share this row block, in order.
+        const int64_t rb0 = int64_t(sg.rb) * p.kt_per_rb;
+        bool ok = true;
+        for (int cc = c - 1; cc >= 0 && range_start(p, cc + 1) > rb0; --cc) {
+          uint32_t* flag = p.flags + 4 * cc + q;
+          int ready = 1;
+          if (lane == 0) {
+            const uint64_t t0 = globaltimer_ns();
+            while (ld_acquire(flag) == 0u) {
+              if (*abort_flag) { ready = 0; break; }
+              if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                *abort_flag = 1;
+                if (p.status) atomicOr(p.status, kStatusEpilogueTimeout);
+                ready = 0;
+                break;
+              }
+            }
+          }
+          ready = __shfl_sync(0xFFFFFFFFu, ready, 0);
+          if (!ready) { ok = false; break; }
+          (void)ld_acquire(flag);
+          const float* src = p.ws + (int64_t(cc) * MPAD) * 128 + n_local;
+#pragma unroll
+          for (int m = 0; m < MPAD; ++m)
+            if (m < p.M) v[m] += __ldcg(src + m * 128);
+          __syncwarp();
+          if (lane == 0) st_release(flag, 0u);
+        }
+        if (!ok) break;
+      }
+      const float a = p.alpha;
+#pragma unroll
+      for (int m = 0; m < MPAD; ++m) {
+        if (m < p.M) {
+          __nv_bfloat16 b = __float2bfloat16_rn(a * v[m]);
+          p.d[int64_t(m) * p.N + n] = *reinterpret_cast<uint16_t*>(&b);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == KT::MmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, KT::TmemCols);
+  }
+#endif  // BLACKHOLE_ARCH_SM100
+}
+
+namespace detail {
+
+template <class KT>
+inline cudaError_t launch_skinny(int M, int N, int K, const void* A, const void* SFA, const void* B,
+                                 const void* SFB, void* D, float alpha, void* ws, int64_t ws_bytes,
+                                 int grid_cap, DeviceState* st, cudaStream_t stream) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  e = set_smem_once(nvfp4_gemm_skinny_kernel<KT>, KT::SmemBytes, dev);
+  if (e != cudaSuccess) return e;
+  Nvfp4SkinnyParams p;
+  e = make_kmajor_tmap(&p.tmap_w, B, N, K / 2, 128);
+  if (e != cudaSuccess) return e;
+  e = make_kmajor_tmap(&p.tmap_x, A, M, K / 2, KT::MPAD);
+  if (e != cudaSuccess) return e;
+  p.kt_per_rb = K / KT::TileK;
+  p.units = int64_t(N / 128) * p.kt_per_rb;
+  int grid = grid_cap < st->num_sms ? grid_cap : st->num_sms;
+  if (p.units < grid) grid = static_cast<int>(p.units);
+  if (nvfp4_skinny_workspace_bytes(st->num_sms, KT::MPAD) > ws_bytes) return cudaErrorInvalidValue;
+  p.sfw = static_cast<const uint8_t*>(SFB);
+  p.sfx = static_cast<const uint8_t*>(SFA);
+  p.d = static_cast<uint16_t*>(D);
+  p.flags = static_cast<uint32_t*>(ws);
+  p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + nvfp4_skinny_flag_bytes(st->num_sms));
+  p.status = st->status;
+  p.alpha = alpha;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.grid = grid;
+  p.sf_k_atoms = static_cast<int>(sf_k_atoms(K));
+  nvfp4_gemm_skinny_kernel<KT><<<grid, KT::NumThreads, KT::SmemBytes, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace detail
+
+// Skinny-M GEMM with a caller-provided workspace of at least
+// nvfp4_skinny_workspace_bytes(num_SMs, nvfp4_skinny_mpad(M)) bytes, zero-filled before its
+// first use (the flag words must start at 0; every launch leaves them at 0).  M in [1, 128].
+inline cudaError_t nvfp4_bf16_gemm_skinny(int M, int N, int K, void const* A, void const* SFA,
+                                          void const* B, void const* SFB, void* D, float alpha,
+                                          void* workspace, int64_t workspace_bytes,
+                                          cudaStream_t stream = nullptr, int grid_cap = 1 << 30) {
+  cudaError_t e = nvfp4_check_args(M, N, K, A, SFA, B, SFB, D);
+  if (e != cudaSuccess) return e;
+  if (M > 128 || !workspace || (reinterpret_cast<uintptr_t>(workspace) & 15u))
+    return cudaErrorInvalidValue;
+  detail::DeviceState* st = detail::prepare_device();
+  if (!st) return cudaErrorInvalidDevice;
+  if (st->init_err != cudaSuccess) return st->init_err;
+  switch (nvfp4_skinny_mpad(M)) {
+    case 16:
+      return detail::launch_skinny<Nvfp4SkinnyTraits<16>>(M, N, K, A, SFA, B, SFB, D, alpha, workspace,
+                                                           workspace_bytes, grid_cap, st, stream);
+    case 32:
+      return detail::launch_skinny<Nvfp4SkinnyTraits<32>>(M, N, K, A, SFA, B, SFB, D, alpha, workspace,
+                                                           workspace_bytes, grid_cap, st, stream);
+    case 64:
+      return detail::launch_skinny<Nvfp4SkinnyTraits<64>>(M, N, K, A, SFA, B, SFB, D, alpha, workspace,
+                                                           workspace_bytes, grid_cap, st, stream);
+    default:
+      return detail::launch_skinny<Nvfp4SkinnyTraits<128>>(M, N, K, A, SFA, B, SFB, D, alpha, workspace,
+                                                            workspace_bytes, grid_cap, st, stream);
+  }
+}
+
+#endif  // __CUDACC__
+
+}  // namespace blackhole::sm100

@@ -76,6 +76,32 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity,
   }
 }
 
+// Warp-uniform form for waits that all 32 lanes of a warp execute: every lane returns the
+// same answer (completion is agreed with __all_sync, giving up is lane 0's decision), so a
+// warp never splits between "done" and "abort" and no later warp-wide operation can hang.
+__device__ __forceinline__ bool wait_bounded_warp(uint32_t bar, uint32_t parity,
+                                                  volatile int* abort_flag, uint32_t* status,
+                                                  uint32_t code) {
+  if (__all_sync(0xFFFFFFFFu, mbar_try_wait(bar, parity))) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (__all_sync(0xFFFFFFFFu, mbar_try_wait(bar, parity))) return true;
+    if ((i & 63u) == 0) {
+      int give_up = 0;
+      if ((threadIdx.x & 31) == 0) {
+        if (*abort_flag) {
+          give_up = 1;
+        } else if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          *abort_flag = 1;
+          if (status) atomicOr(status, code);
+          give_up = 1;
+        }
+      }
+      if (__shfl_sync(0xFFFFFFFFu, give_up, 0)) return false;
+    }
+  }
+}
+
 // ---- TMA / bulk copies -------------------------------------------------------------------
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
@@ -187,18 +213,178 @@ __device__ __forceinline__ void reg_fence(uint32_t (&r)[32]) {
   for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(r[i]));
 }
 
+// ---- warp-wide issue forms ------------------------------------------------------------------
+// The MMA warp computes every operand (descriptors, TMEM addresses) with all 32 lanes, so
+// the values are warp-uniform, and each tcgen05 instruction is issued by the lane that
+// elect.sync picks inside the asm.  Measured on B200: a k-tile of 12 scale-factor copies +
+// 4 MMAs (128x256x64) issues in 513 clocks this way, i.e. at the MMA rate, against 914
+// clocks when lane 0 alone computes and issues.  All 32 lanes must call these together; the
+// same lane is elected every time, so commits track that lane's MMAs.
+__device__ __forceinline__ void tc_cp_32x128b_warpx4_w(uint32_t taddr, uint64_t sdesc) {
+  asm volatile(
+      "{\n\t.reg .pred P;\n\telect.sync _|P, 0xffffffff;\n\t"
+      "@P tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;\n\t}" ::"r"(taddr),
+      "l"(sdesc)
+      : "memory");
+}
+__device__ __forceinline__ void tc_mma_nvf4_w(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                              uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, P;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync _|P, 0xffffffff;\n\t"
+      "@P tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t"
+      "}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit_w(uint32_t bar) {
+  asm volatile(
+      "{\n\t.reg .pred P;\n\telect.sync _|P, 0xffffffff;\n\t"
+      "@P tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tc_cp_32x128b_warpx4_pair_w(uint32_t taddr, uint64_t sdesc) {
+  asm volatile(
+      "{\n\t.reg .pred P;\n\telect.sync _|P, 0xffffffff;\n\t"
+      "@P tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;\n\t}" ::"r"(taddr),
+      "l"(sdesc)
+      : "memory");
+}
+__device__ __forceinline__ void tc_mma_nvf4_pair_w(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                                   uint32_t idesc, uint32_t sfa_tmem,
+                                                   uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, P;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync _|P, 0xffffffff;\n\t"
+      "@P tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t"
+      "}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit_pair_w(uint32_t cluster_bar) {
+  asm volatile(
+      "{\n\t.reg .pred P;\n\telect.sync _|P, 0xffffffff;\n\t"
+      "@P tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+          cluster_bar)
+      : "memory");
+}
+
+// ---- clusters and the 2-SM (cta_group::2) datapath ---------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory offset in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+// Arrive on an mbarrier of any CTA in the cluster (shared::cluster address).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+// 2-D tiled TMA load into this CTA's shared memory whose completion is counted on an
+// mbarrier of the pair's leader CTA (cluster address `leader_bar`).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* m,
+                                                 uint32_t leader_bar, int32_t x, int32_t y,
+                                                 uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(leader_bar), "r"(x), "r"(y), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+// Arrive on `cluster_bar` (any CTA of the pair) when the pair's MMAs issued so far are done.
+__device__ __forceinline__ void tc_commit_pair(uint32_t cluster_bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   cluster_bar)
+               : "memory");
+}
+// Scale-factor atom copy into both CTAs of the pair (each from its own shared memory).
+__device__ __forceinline__ void tc_cp_32x128b_warpx4_pair(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc)
+               : "memory");
+}
+// 256 x N x 64 block-scaled MMA over the CTA pair (issued by the leader only).
+__device__ __forceinline__ void tc_mma_nvf4_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                                 uint32_t idesc, uint32_t sfa_tmem,
+                                                 uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t"
+      "}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+// ---- TMA stores ----------------------------------------------------------------------------
+// 2-D tiled TMA store from this CTA's shared memory (bulk-group completion).  Coordinates
+// must be non-negative; the part of the box outside the tensor is not written.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, uint32_t src, int32_t x,
+                                             int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(src), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Waits until at most N committed bulk groups of this thread still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait_group() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+
 // ---- shared-memory matrix descriptors (tcgen05 format, version 1) -----------------------
-// K-major operand tile stored as 128-byte rows with the 128B swizzle (as TMA writes it with
-// CU_TENSOR_MAP_SWIZZLE_128B); 8-row groups are 1024 bytes apart.
-__device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t saddr) {
+// K-major operand tile stored as ROW_BYTES-byte rows with the matching swizzle (as TMA writes
+// it with CU_TENSOR_MAP_SWIZZLE_128B / _64B / _32B); 8-row groups are 8 * ROW_BYTES apart.
+template <int ROW_BYTES>
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t saddr) {
+  static_assert(ROW_BYTES == 128 || ROW_BYTES == 64 || ROW_BYTES == 32, "swizzle width");
+  constexpr uint64_t layout = ROW_BYTES == 128 ? 2 : (ROW_BYTES == 64 ? 4 : 6);
   uint64_t d = 0;
   d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);  // start address, 16-byte units
   d |= static_cast<uint64_t>(1) << 16;                 // leading byte offset (unused here)
-  d |= static_cast<uint64_t>(1024 >> 4) << 32;         // stride byte offset: 8 rows
+  d |= static_cast<uint64_t>((8 * ROW_BYTES) >> 4) << 32;  // stride byte offset: 8 rows
   d |= static_cast<uint64_t>(1) << 46;                 // descriptor version (sm_100)
-  d |= static_cast<uint64_t>(2) << 61;                 // layout: SWIZZLE_128B
+  d |= layout << 61;                                   // swizzle mode
   return d;
 }
+__device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t saddr) { return desc_kmajor<128>(saddr); }
 // Unswizzled 32-row x 16-byte block (a scale-factor atom): 8-row core matrices 128 B apart.
 __device__ __forceinline__ uint64_t desc_sf_atom(uint32_t saddr) {
   uint64_t d = 0;

@@ -42,6 +42,24 @@ BLACKHOLE_SM100_API int blackhole_sm100_nvfp4_bf16_gemm(int M, int N, int K, con
                                     const void* B, const void* SFB, void* D, float alpha,
                                     cudaStream_t stream);
 
+/* Same GEMM with an explicit schedule and workspace (no counterpart in the reference, which
+ * has a single schedule).  schedule: 0 = by shape (as above), 1 = one-SM 128x256 tiles,
+ * 2 = two-SM 256x256 tiles (cta_group::2), 3 = skinny-M stream-K (M <= 128).
+ * workspace: device memory for the skinny schedule, at least
+ * blackhole_sm100_workspace_bytes(M, N, K) bytes, zero-filled before its first use and left
+ * zeroed by every call; NULL selects a library-owned buffer per (device, stream), allocated
+ * on first use.  Calls that share one workspace must be ordered (same stream). */
+BLACKHOLE_SM100_API int blackhole_sm100_nvfp4_bf16_gemm_ex(int M, int N, int K, const void* A,
+                                                           const void* SFA, const void* B,
+                                                           const void* SFB, void* D, float alpha,
+                                                           int schedule, void* workspace,
+                                                           int64_t workspace_bytes,
+                                                           cudaStream_t stream);
+
+/* Workspace bytes blackhole_sm100_nvfp4_bf16_gemm_ex needs for this shape on the current
+ * device (0 when the shape does not use the skinny schedule); negative on error. */
+BLACKHOLE_SM100_API int64_t blackhole_sm100_workspace_bytes(int M, int N, int K);
+
 /* Bytes of a (mn x k) scale-factor tensor in the 128x4 layout, padding included
  * (the cosize of make_layout_SFA/SFB; nvfp4_gemm.hpp:293-302). */
 BLACKHOLE_SM100_API int64_t blackhole_sm100_sf_storage_bytes(int64_t mn, int64_t k);

@@ -19,7 +19,7 @@ def make_operands(M, N, K, seed=0, std_a=1.0, std_b=1.0, outlier_p=0.0, outlier_
     return A, SFA, B, SFB, alpha
 
 
-def run_gpu(M, N, K, A, SFA, B, SFB, alpha, repeat=1):
+def run_gpu(M, N, K, A, SFA, B, SFB, alpha, repeat=1, schedule="auto", workspace=None):
     """Runs the CUDA GEMM through the C ABI; returns D as uint16 bf16 bits [M, N]."""
     import torch
     import blackhole_b200 as bh
@@ -32,7 +32,11 @@ def run_gpu(M, N, K, A, SFA, B, SFB, alpha, repeat=1):
     D = torch.full((M, N), -1, dtype=torch.int16, device=dev)  # NaN pattern: catches unwritten
     outs = []
     for _ in range(repeat):
-        bh.nvfp4_bf16_gemm(M, N, K, tA, tSFA, tB, tSFB, D, alpha)
+        if schedule == "auto" and workspace is None:
+            bh.nvfp4_bf16_gemm(M, N, K, tA, tSFA, tB, tSFB, D, alpha)
+        else:
+            bh.nvfp4_bf16_gemm_ex(M, N, K, tA, tSFA, tB, tSFB, D, alpha, schedule=schedule,
+                                  workspace=workspace)
         torch.cuda.synchronize()
         outs.append(D.cpu().numpy().view(np.uint16).copy())
     assert bh.device_status(0) == 0
