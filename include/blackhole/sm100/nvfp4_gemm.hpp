@@ -17,10 +17,10 @@
 // Schedules (chosen by shape):
 //   * M <= 128 : skinny schedule (nvfp4_gemm_skinny.hpp) -- swap-AB, stream-K over all SMs,
 //                HBM-bound; needs a small FP32 workspace (allocated here per device and
-//                stream on first use, or passed by the caller: nvfp4_bf16_gemm_ws);
-//   * M > 128  : two-SM schedule (nvfp4_gemm_2sm.hpp) -- 256 x 256 tiles per CTA pair,
-//                tensor-bound;
-//   * the one-SM schedule (nvfp4_gemm_1sm.hpp, 128 x 256 tiles) is available explicitly.
+//                stream on first use, or passed by the caller: nvfp4_bf16_gemm_ex);
+//   * M > 128  : one-SM schedule (nvfp4_gemm_1sm.hpp) -- 128 x 256 tiles, tensor-bound;
+//   * the two-SM schedule (nvfp4_gemm_2sm.hpp, 256 x 256 tiles per CTA pair) is available
+//     explicitly (on B200 it measured slower than the one-SM schedule at 8192^3).
 //
 // Shapes: M >= 1, N % 128 == 0, K % 256 == 0.  The reference additionally requires
 // M % 128 == 0 (nvfp4_gemm.hpp:594).  Every mbarrier wait in the kernels is bounded: a
@@ -102,7 +102,7 @@ inline cudaError_t nvfp4_bf16_gemm_ex(int M, int N, int K, void const* A, void c
   e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (schedule == Nvfp4Schedule::kAuto)
-    schedule = M <= 128 ? Nvfp4Schedule::kSkinny : Nvfp4Schedule::kTwoSm;
+    schedule = M <= 128 ? Nvfp4Schedule::kSkinny : Nvfp4Schedule::kOneSm;
   switch (schedule) {
     case Nvfp4Schedule::kOneSm:
       return detail::launch_1sm<Nvfp4GemmTraits>(M, N, K, A, SFA, B, SFB, D, alpha, st, dev, stream);

@@ -13,7 +13,8 @@
 //                    smem stage; after the last k-tile it signals the epilogue.
 //   warps 2-9 (epi): tcgen05.ld the accumulator (two warps per 32-lane sub-partition, 128
 //                    columns each), release TMEM to the MMA warp at once, then alpha * acc
-//                    -> BF16 -> global while the next tile's mainloop runs.
+//                    -> BF16 through a 1 KB swizzled shared-memory box per warp and TMA
+//                    tensor stores while the next tile's mainloop runs.
 // Used for small problems; large ones take the two-SM schedule (nvfp4_gemm_2sm.hpp).
 // =====================================================================================
 
@@ -49,20 +50,25 @@ struct Nvfp4GemmTraitsT {
   static constexpr int FirstEpiWarp = 2;
   static constexpr int NumEpiWarps = 8;
 
-  // TMEM columns: accumulator [0,256), SFA 4 per k-step, SFB 8 per k-step.
+  // TMEM columns: accumulator [0,256); scale factors after it: SFA (4 columns per k-step)
+  // then SFB (8 per k-step).
   static constexpr uint32_t TmemCols = 512;
   static constexpr uint32_t AccCol = 0;
-  static constexpr uint32_t SfaCol = 256;
-  static constexpr uint32_t SfbCol = SfaCol + 4 * KSteps;
+  static constexpr uint32_t SfCol = 256;
+  static constexpr uint32_t SfStride = 12 * KSteps;
 
-  // shared memory: stage ring + barriers (+1 KB to align the ring to 1024 B)
+  // epilogue staging: one 32-row x 16-column BF16 box (1 KB, 32B-swizzled) per epilogue warp
+  static constexpr int StoreBoxBytes = 32 * 16 * 2;
+  static constexpr int StagingBytes = NumEpiWarps * StoreBoxBytes;
+
+  // shared memory: stage ring + staging + barriers (+1 KB to align the ring to 1024 B)
   static constexpr int BarrierBytes = 8 * (2 * Stages + 4) + 16;
-  static constexpr int SmemBytes = Stages * StageBytes + BarrierBytes + 1024;
+  static constexpr int SmemBytes = Stages * StageBytes + StagingBytes + BarrierBytes + 1024;
 
   static constexpr int RasterGroupM = 16;  // tiles walk 16 M-blocks at a time (L2 reuse)
 
   static_assert(SmemBytes <= arch_traits<Arch::kSm100>::max_smem_per_cta, "smem budget");
-  static_assert(SfbCol + 8 * KSteps <= TmemCols, "TMEM budget");
+  static_assert(SfCol + 2 * SfStride <= TmemCols, "TMEM budget");
 };
 using Nvfp4GemmTraits = Nvfp4GemmTraitsT<256, 4>;
 
@@ -74,9 +80,9 @@ using Nvfp4GemmTraits = Nvfp4GemmTraitsT<256, 4>;
 struct Nvfp4GemmParams {
   CUtensorMap tmap_a;   // A as uint8 [M][K/2], box 128 x 128 B, 128B swizzle
   CUtensorMap tmap_b;   // B as uint8 [N][K/2], box 256 x 128 B, 128B swizzle
+  CUtensorMap tmap_d;   // D bf16 [M][N], box 32 rows x 16 columns, 32B swizzle
   const uint8_t* sfa;
   const uint8_t* sfb;
-  uint16_t* d;
   uint32_t* status;
   float alpha;
   int M, N, K;
@@ -119,7 +125,8 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
   const uint32_t sB = sA + S * KT::ABytes;
   const uint32_t sSFA = sB + S * KT::BBytes;
   const uint32_t sSFB = sSFA + S * KT::SFABytes;
-  const uint32_t bars = sSFB + S * KT::SFBBytes;
+  const uint32_t sStage = sSFB + S * KT::SFBBytes;  // epilogue staging boxes
+  const uint32_t bars = sStage + KT::StagingBytes;
   auto full_bar = [&](int s) { return bars + 8u * s; };
   auto empty_bar = [&](int s) { return bars + 8u * (S + s); };
   const uint32_t acc_full = bars + 16u * S;
@@ -150,6 +157,7 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
   if (warp == KT::ProducerWarp && lane == 0) {
     prefetch_tmap(&p.tmap_a);
     prefetch_tmap(&p.tmap_b);
+    prefetch_tmap(&p.tmap_d);
   }
   tc_fence_before();
   __syncthreads();
@@ -211,49 +219,65 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
     }
   } else if (warp == KT::MmaWarp) {
     // ------------------------------ MMA issuer --------------------------------------
+    // Per k-tile: probe the next stage's barrier, copy this stage's scale factors to TMEM,
+    // four MMAs, commit, then consume the probe (falling back to a bounded wait).
     constexpr uint32_t idesc = idesc_nvf4(KT::TileM, KT::TileN);
     int stage = 0;
     uint32_t phase = 0;
     uint32_t acc_phase = 0;
+    const uint32_t sfbuf = 0;
     bool ok = true;
     bool issued_any = false;
+    auto copy_sf = [&](int st, uint32_t b) {
+      const uint32_t sfa_s = sSFA + st * KT::SFABytes;
+      const uint32_t sfb_s = sSFB + st * KT::SFBBytes;
+      const uint32_t ta = tmem + KT::SfCol + KT::SfStride * b;
+#pragma unroll
+      for (int j = 0; j < KT::KSteps; ++j) {
+        tc_cp_32x128b_warpx4_w(ta + 4 * j, desc_sf_atom(sfa_s + 512 * j));
+        tc_cp_32x128b_warpx4_w(ta + 4 * KT::KSteps + 8 * j, desc_sf_atom(sfb_s + 512 * j));
+        tc_cp_32x128b_warpx4_w(ta + 4 * KT::KSteps + 8 * j + 4,
+                               desc_sf_atom(sfb_s + KT::SFBBytes / 2 + 512 * j));
+      }
+    };
     for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
       if (!wait_bounded_warp(acc_empty, acc_phase ^ 1u, abort_flag, p.status, kStatusMmaTimeout)) {
         ok = false;
         break;
       }
       tc_fence_after();
+      // the first stage of a tile is waited for; each later one is probed one k-tile ahead
+      if (!wait_bounded_warp(full_bar(stage), phase, abort_flag, p.status, kStatusMmaTimeout)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
       for (int kt = 0; kt < p.k_tiles; ++kt) {
-        if (!wait_bounded_warp(full_bar(stage), phase, abort_flag, p.status, kStatusMmaTimeout)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        {
-          const uint32_t sfa_s = sSFA + stage * KT::SFABytes;
-          const uint32_t sfb_s = sSFB + stage * KT::SFBBytes;
+        const int nstage = stage + 1 == S ? 0 : stage + 1;
+        const uint32_t nphase = stage + 1 == S ? (phase ^ 1u) : phase;
+        const bool more = kt + 1 < p.k_tiles;
+        const uint32_t ready = more ? mbar_probe(full_bar(nstage), nphase) : 1u;
+        copy_sf(stage, sfbuf);
+        const uint64_t adesc = desc_kmajor<KT::RowBytes>(sA + stage * KT::ABytes);
+        const uint64_t bdesc = desc_kmajor<KT::RowBytes>(sB + stage * KT::BBytes);
+        const uint32_t ta = tmem + KT::SfCol + KT::SfStride * sfbuf;
 #pragma unroll
-          for (int j = 0; j < KT::KSteps; ++j) {
-            tc_cp_32x128b_warpx4_w(tmem + KT::SfaCol + 4 * j, desc_sf_atom(sfa_s + 512 * j));
-            tc_cp_32x128b_warpx4_w(tmem + KT::SfbCol + 8 * j, desc_sf_atom(sfb_s + 512 * j));
-            tc_cp_32x128b_warpx4_w(tmem + KT::SfbCol + 8 * j + 4,
-                                   desc_sf_atom(sfb_s + KT::SFBBytes / 2 + 512 * j));
-          }
-          const uint64_t adesc = desc_kmajor<KT::RowBytes>(sA + stage * KT::ABytes);
-          const uint64_t bdesc = desc_kmajor<KT::RowBytes>(sB + stage * KT::BBytes);
-#pragma unroll
-          for (int j = 0; j < KT::KSteps; ++j) {
-            // +32 bytes of K per step inside the 128-byte swizzle row (descriptor units: 16 B)
-            tc_mma_nvf4_w(tmem + KT::AccCol, adesc + 2 * j, bdesc + 2 * j, idesc,
-                          tmem + KT::SfaCol + 4 * j, tmem + KT::SfbCol + 8 * j,
-                          (kt | j) != 0 ? 1u : 0u);
-          }
-          tc_commit_w(empty_bar(stage));
-          issued_any = true;
+        for (int j = 0; j < KT::KSteps; ++j) {
+          // +32 bytes of K per step inside the swizzled row (descriptor units: 16 B)
+          tc_mma_nvf4_w(tmem + KT::AccCol, adesc + 2 * j, bdesc + 2 * j, idesc, ta + 4 * j,
+                        ta + 4 * KT::KSteps + 8 * j, (kt | j) != 0 ? 1u : 0u);
         }
-        if (++stage == S) {
-          stage = 0;
-          phase ^= 1u;
+        tc_commit_w(empty_bar(stage));
+        issued_any = true;
+        stage = nstage;
+        phase = nphase;
+        if (more) {
+          if (!__all_sync(0xFFFFFFFFu, ready != 0u) &&
+              !wait_bounded_warp(full_bar(stage), phase, abort_flag, p.status, kStatusMmaTimeout)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
         }
       }
       if (!ok) break;
@@ -292,27 +316,46 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
       if (lane == 0) mbar_arrive(acc_empty);
       acc_phase ^= 1u;
 
-      const int row = m_blk * KT::TileM + 32 * q + lane;
+      // alpha * acc -> BF16 -> this warp's 1 KB staging box -> TMA store, 16 columns at a
+      // time.  Lane i owns row i (32 bytes); its 16-byte chunk c lands at chunk
+      // c ^ ((i / 4) % 2), the layout CU_TENSOR_MAP_SWIZZLE_32B expects.
+      const int row0 = m_blk * KT::TileM + 32 * q;
       const int col0 = n_blk * KT::TileN + 128 * half;
-      if (row < p.M && col0 < p.N) {
-        uint16_t* dst = p.d + static_cast<int64_t>(row) * p.N + col0;
-        const float a = p.alpha;
-        auto emit = [&](uint32_t (&v)[32], int c) {
+      const uint32_t box = sStage + (warp - KT::FirstEpiWarp) * KT::StoreBoxBytes;
+      const uint32_t my_row = box + lane * 32;
+      const uint32_t sw = (lane >> 2) & 1;
+      const float a = p.alpha;
+      const bool live = row0 < p.M && col0 < p.N;
+      const uint64_t pol_d = l2_policy_evict_first();   // keep A / B resident in L2
+      auto stage_store = [&](uint32_t (&v)[32], int c32) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            st_global_v4(dst + c + i,
+        for (int h = 0; h < 2; ++h) {
+          if (lane == 0) bulk_wait_group_read<0>();   // previous box has been read out
+          __syncwarp();
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const int i = 16 * h + 8 * c;
+            st_shared_v4(my_row + ((c ^ sw) << 4),
                          detail::pack_bf16x2(a * __uint_as_float(v[i + 0]), a * __uint_as_float(v[i + 1])),
                          detail::pack_bf16x2(a * __uint_as_float(v[i + 2]), a * __uint_as_float(v[i + 3])),
                          detail::pack_bf16x2(a * __uint_as_float(v[i + 4]), a * __uint_as_float(v[i + 5])),
                          detail::pack_bf16x2(a * __uint_as_float(v[i + 6]), a * __uint_as_float(v[i + 7])));
           }
-        };
-        emit(v0, 0);
-        emit(v1, 32);
-        emit(v2, 64);
-        emit(v3, 96);
-      }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && live) {
+            tma_store_2d(&p.tmap_d, box, col0 + c32 + 16 * h, row0, pol_d);
+            bulk_commit_group();
+          }
+        }
+      };
+      stage_store(v0, 0);
+      stage_store(v1, 32);
+      stage_store(v2, 64);
+      stage_store(v3, 96);
     }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -337,9 +380,10 @@ inline cudaError_t launch_1sm(int M, int N, int K, const void* A, const void* SF
   if (e != cudaSuccess) return e;
   e = make_kmajor_tmap(&p.tmap_b, B, N, K / 2, KT::TileN, KT::RowBytes);
   if (e != cudaSuccess) return e;
+  e = make_d_tmap(&p.tmap_d, D, M, N, 16);
+  if (e != cudaSuccess) return e;
   p.sfa = static_cast<const uint8_t*>(SFA);
   p.sfb = static_cast<const uint8_t*>(SFB);
-  p.d = static_cast<uint16_t*>(D);
   p.status = st->status;
   p.alpha = alpha;
   p.M = M;

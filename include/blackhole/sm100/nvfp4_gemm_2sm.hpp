@@ -53,10 +53,12 @@ struct Nvfp4Gemm2SmTraitsT {
   static constexpr int FirstEpiWarp = 2;
   static constexpr int NumEpiWarps = 8;
 
+  // TMEM columns: accumulator [0,256); scale factors after it: SFA (4 columns per k-step)
+  // then SFB (8 per k-step).
   static constexpr uint32_t TmemCols = 512;
   static constexpr uint32_t AccCol = 0;
-  static constexpr uint32_t SfaCol = 256;
-  static constexpr uint32_t SfbCol = SfaCol + 4 * KSteps;
+  static constexpr uint32_t SfCol = 256;
+  static constexpr uint32_t SfStride = 12 * KSteps;
 
   // epilogue staging: one 32-row x 64-column BF16 box (4 KB, 128B-swizzled) per epilogue warp
   static constexpr int StoreBoxBytes = 32 * 64 * 2;
@@ -210,6 +212,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
     }
   } else if (warp == KT::MmaWarp) {
     // ------------------------------ MMA issuer (leader CTA) -------------------------
+    // Per k-tile: probe the next stage's barrier, copy this stage's scale factors to TMEM,
+    // four MMAs, commit, then consume the probe (falling back to a bounded wait).
     if (rank == 0) {
       constexpr uint32_t idesc = idesc_nvf4(KT::TileM, KT::TileN);
       const uint32_t acc_full_0 = mapa_shared(acc_full, 0);
@@ -217,45 +221,59 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t acc_phase = 0;
+      const uint32_t sfbuf = 0;
       bool ok = true;
       bool issued_any = false;
+      auto copy_sf = [&](int st, uint32_t b) {
+        const uint32_t sfa_s = sSFA + st * KT::SFABytes;
+        const uint32_t sfb_s = sSFB + st * KT::SFBBytes;
+        const uint32_t ta = tmem + KT::SfCol + KT::SfStride * b;
+#pragma unroll
+        for (int j = 0; j < KT::KSteps; ++j) {
+          tc_cp_32x128b_warpx4_pair_w(ta + 4 * j, desc_sf_atom(sfa_s + 512 * j));
+          tc_cp_32x128b_warpx4_pair_w(ta + 4 * KT::KSteps + 8 * j, desc_sf_atom(sfb_s + 512 * j));
+          tc_cp_32x128b_warpx4_pair_w(ta + 4 * KT::KSteps + 8 * j + 4,
+                                      desc_sf_atom(sfb_s + KT::SFBBytes / 2 + 512 * j));
+        }
+      };
       for (int tile = cluster; ok && tile < p.num_tiles; tile += num_clusters) {
         if (!wait_bounded_warp(acc_empty, acc_phase ^ 1u, abort_flag, p.status, kStatusMmaTimeout)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        // the first stage of a tile is waited for; each later one is probed one k-tile ahead
+        if (!wait_bounded_warp(full_bar(stage), phase, abort_flag, p.status, kStatusMmaTimeout)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
         for (int kt = 0; kt < p.k_tiles; ++kt) {
-          if (!wait_bounded_warp(full_bar(stage), phase, abort_flag, p.status, kStatusMmaTimeout)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          {
-            const uint32_t sfa_s = sSFA + stage * KT::SFABytes;
-            const uint32_t sfb_s = sSFB + stage * KT::SFBBytes;
+          const int nstage = stage + 1 == S ? 0 : stage + 1;
+          const uint32_t nphase = stage + 1 == S ? (phase ^ 1u) : phase;
+          const bool more = kt + 1 < p.k_tiles;
+          const uint32_t ready = more ? mbar_probe(full_bar(nstage), nphase) : 1u;
+          copy_sf(stage, sfbuf);
+          const uint64_t adesc = desc_kmajor<KT::RowBytes>(sA + stage * KT::ABytes);
+          const uint64_t bdesc = desc_kmajor<KT::RowBytes>(sB + stage * KT::BBytes);
+          const uint32_t ta = tmem + KT::SfCol + KT::SfStride * sfbuf;
 #pragma unroll
-            for (int j = 0; j < KT::KSteps; ++j) {
-              tc_cp_32x128b_warpx4_pair_w(tmem + KT::SfaCol + 4 * j, desc_sf_atom(sfa_s + 512 * j));
-              tc_cp_32x128b_warpx4_pair_w(tmem + KT::SfbCol + 8 * j, desc_sf_atom(sfb_s + 512 * j));
-              tc_cp_32x128b_warpx4_pair_w(tmem + KT::SfbCol + 8 * j + 4,
-                                          desc_sf_atom(sfb_s + KT::SFBBytes / 2 + 512 * j));
-            }
-            const uint64_t adesc = desc_kmajor<KT::RowBytes>(sA + stage * KT::ABytes);
-            const uint64_t bdesc = desc_kmajor<KT::RowBytes>(sB + stage * KT::BBytes);
-#pragma unroll
-            for (int j = 0; j < KT::KSteps; ++j) {
-              tc_mma_nvf4_pair_w(tmem + KT::AccCol, adesc + 2 * j, bdesc + 2 * j, idesc,
-                                 tmem + KT::SfaCol + 4 * j, tmem + KT::SfbCol + 8 * j,
-                                 (kt | j) != 0 ? 1u : 0u);
-            }
-            tc_commit_pair_w(mapa_shared(empty_bar(stage), 0));
-            tc_commit_pair_w(mapa_shared(empty_bar(stage), 1));
-            issued_any = true;
+          for (int j = 0; j < KT::KSteps; ++j) {
+            tc_mma_nvf4_pair_w(tmem + KT::AccCol, adesc + 2 * j, bdesc + 2 * j, idesc, ta + 4 * j,
+                               ta + 4 * KT::KSteps + 8 * j, (kt | j) != 0 ? 1u : 0u);
           }
-          if (++stage == S) {
-            stage = 0;
-            phase ^= 1u;
+          tc_commit_pair_w(mapa_shared(empty_bar(stage), 0));
+          tc_commit_pair_w(mapa_shared(empty_bar(stage), 1));
+          issued_any = true;
+          stage = nstage;
+          phase = nphase;
+          if (more) {
+            if (!__all_sync(0xFFFFFFFFu, ready != 0u) &&
+                !wait_bounded_warp(full_bar(stage), phase, abort_flag, p.status, kStatusMmaTimeout)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
           }
         }
         if (!ok) break;
@@ -304,6 +322,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
       const uint32_t box = sStage + (warp - KT::FirstEpiWarp) * KT::StoreBoxBytes;
       const uint32_t my_row = box + lane * 128;
       const float a = p.alpha;
+      const uint64_t pol_d = l2_policy_evict_first();   // keep A / B resident in L2
       auto stage_store = [&](uint32_t (&va)[32], uint32_t (&vb)[32], int u) {
         if (lane == 0) bulk_wait_group_read<0>();   // previous box has been read out
         __syncwarp();
@@ -320,7 +339,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0 && row0 < p.M && col0 + 64 * u < p.N) {
-          tma_store_2d(&p.tmap_d, box, col0 + 64 * u, row0);
+          tma_store_2d(&p.tmap_d, box, col0 + 64 * u, row0, pol_d);
           bulk_commit_group();
         }
       };

@@ -120,17 +120,22 @@ inline cudaError_t make_sf_tmap(CUtensorMap* m, const void* base, int64_t mn, in
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-// Row-major BF16 [rows][cols] output with a (32 rows x 64 columns) box, 128B swizzle: the
-// store box of one epilogue warp.  Parts of a box past the tensor edge are not written.
-inline cudaError_t make_d_tmap(CUtensorMap* m, void* base, int64_t rows, int64_t cols) {
+// Row-major BF16 [rows][cols] output with a (32 rows x box_cols columns) box: the store box
+// of one epilogue warp.  Parts of a box past the tensor edge are not written.
+// box_cols = 64 (128-byte rows, 128B swizzle) or 16 (32-byte rows, 32B swizzle).
+inline cudaError_t make_d_tmap(CUtensorMap* m, void* base, int64_t rows, int64_t cols,
+                               uint32_t box_cols = 64) {
   EncodeTiledFn enc = encode_tiled_fn();
   if (!enc) return cudaErrorNotSupported;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * 2)};
-  cuuint32_t box[2] = {64u, 32u};
+  cuuint32_t box[2] = {box_cols, 32u};
   cuuint32_t estr[2] = {1u, 1u};
+  const CUtensorMapSwizzle swz = box_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                 : box_cols == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                  : CU_TENSOR_MAP_SWIZZLE_32B;
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }

@@ -268,12 +268,16 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
       }
       tc_fence_after();
       const uint32_t d_tmem = tmem + KT::AccStride * acc;
+      if (!wait_bounded_warp(full_bar(stage), phase, abort_flag, p.status, kStatusMmaTimeout)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
       for (int kt = sg.kt0; kt < sg.kt1; ++kt) {
-        if (!wait_bounded_warp(full_bar(stage), phase, abort_flag, p.status, kStatusMmaTimeout)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
+        const int nstage = stage + 1 == S ? 0 : stage + 1;
+        const uint32_t nphase = stage + 1 == S ? (phase ^ 1u) : phase;
+        const bool more = kt + 1 < sg.kt1;
+        const uint32_t ready = more ? mbar_probe(full_bar(nstage), nphase) : 1u;
         {
 #pragma unroll
           for (int j = 0; j < KT::KSteps; ++j) {
@@ -290,9 +294,15 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
           tc_commit_w(empty_bar(stage));
           issued_any = true;
         }
-        if (++stage == S) {
-          stage = 0;
-          phase ^= 1u;
+        stage = nstage;
+        phase = nphase;
+        if (more) {
+          if (!__all_sync(0xFFFFFFFFu, ready != 0u) &&
+              !wait_bounded_warp(full_bar(stage), phase, abort_flag, p.status, kStatusMmaTimeout)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
         }
       }
       if (!ok) break;
