@@ -16,7 +16,7 @@ import os
 __all__ = [
     "LIB_PATH", "load", "nvfp4_bf16_gemm", "sf_storage_bytes", "sf_offset",
     "device_status", "BlackholeError", "nvfp4_quantize", "quantize_tensor",
-    "nvfp4_bf16_gemm_ex", "workspace_bytes", "SCHEDULES",
+    "nvfp4_bf16_gemm_ex", "workspace_bytes", "SCHEDULES", "nvfp4_bf16_gemm_noalloc",
 ]
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -53,6 +53,9 @@ def load():
     L.blackhole_sm100_nvfp4_bf16_gemm_ex.restype = i32
     L.blackhole_sm100_nvfp4_bf16_gemm_ex.argtypes = [i32, i32, i32, vp, vp, vp, vp, vp, ctypes.c_float,
                                                      i32, vp, i64, vp]
+    L.blackhole_sm100_nvfp4_bf16_gemm_noalloc.restype = i32
+    L.blackhole_sm100_nvfp4_bf16_gemm_noalloc.argtypes = [i32, i32, i32, vp, vp, vp, vp, vp,
+                                                          ctypes.c_float, vp]
     L.blackhole_sm100_workspace_bytes.restype = i64
     L.blackhole_sm100_workspace_bytes.argtypes = [i32, i32, i32]
     L.blackhole_sm100_sf_storage_bytes.restype = i64
@@ -127,6 +130,19 @@ def nvfp4_bf16_gemm_ex(M: int, N: int, K: int, A, SFA, B, SFB, D, alpha: float =
         int(workspace_bytes), _stream(stream))
     if rc != 0:
         raise BlackholeError("blackhole_sm100_nvfp4_bf16_gemm_ex", rc)
+
+
+def nvfp4_bf16_gemm_noalloc(M: int, N: int, K: int, A, SFA, B, SFB, D, alpha: float = 1.0,
+                            stream=None) -> None:
+    """The GEMM for M <= 16 without any device allocation, for callers that must not
+    allocate at call time.  Its scratch lives in a fixed array inside the library (sized for
+    M <= 16 on up to 160 SMs), shared by every call: calls that overlap on the GPU race.
+    The first call on a device resolves the array's address; make it before any capture."""
+    rc = load().blackhole_sm100_nvfp4_bf16_gemm_noalloc(
+        int(M), int(N), int(K), _ptr(A), _ptr(SFA), _ptr(B), _ptr(SFB), _ptr(D), float(alpha),
+        _stream(stream))
+    if rc != 0:
+        raise BlackholeError("blackhole_sm100_nvfp4_bf16_gemm_noalloc", rc)
 
 
 def workspace_bytes(M: int, N: int, K: int) -> int:

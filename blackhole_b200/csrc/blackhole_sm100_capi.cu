@@ -7,6 +7,55 @@
 #include <blackhole/sm100/nvfp4_gemm.hpp>
 #include <blackhole/sm100/nvfp4_quant.hpp>
 
+#include <mutex>
+
+// ---------------------------------------------------------------------------------------
+// Allocation-free skinny GEMM (blackhole_sm100_nvfp4_bf16_gemm_noalloc).
+//
+// Some callers cannot allocate device memory at the point where they run the GEMM: serving
+// engines that reserve all device memory at start-up and forbid allocation afterwards,
+// latency-critical paths that must not pay cudaMalloc's implicit device synchronisation,
+// and plugin hosts that hand a plugin nothing but its input and output buffers.  The
+// skinny schedule needs scratch (one flag word per epilogue warp and an FP32 partial tile
+// per CTA), so this entry point keeps that scratch in a fixed array of this module instead.
+//
+// The array holds what M <= 16 needs on a device with up to 160 SMs:
+//   flags    : 160 CTAs x 4 warps x 4 bytes = 2560 bytes (already a multiple of 256)
+//   partials : 160 CTAs x 16 rows x 128 columns x 4 bytes = 1,310,720 bytes
+// Every GPU that loads this library holds these 1,313,280 bytes until the process exits.
+// ---------------------------------------------------------------------------------------
+namespace {
+
+constexpr int kNoAllocMaxM = 16;
+constexpr int kNoAllocMaxSms = 160;
+constexpr size_t kNoAllocScratchBytes =
+    size_t(kNoAllocMaxSms) * 16 + size_t(kNoAllocMaxSms) * kNoAllocMaxM * 128 * 4;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// The symbol above names a host-side stand-in, not a device address, so the kernel must be
+// given the address that cudaGetSymbolAddress returns for the current device.
+struct NoAllocDevice {
+  std::once_flag once;
+  cudaError_t err = cudaSuccess;
+  void* scratch = nullptr;
+};
+
+cudaError_t noalloc_scratch(void** out) {
+  static NoAllocDevice devs[64];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  NoAllocDevice& d = devs[dev];
+  std::call_once(d.once, [&]() { d.err = cudaGetSymbolAddress(&d.scratch, g_noalloc_scratch); });
+  if (d.err != cudaSuccess) return d.err;
+  *out = d.scratch;
+  return cudaSuccess;
+}
+
+}  // namespace
+
 extern "C" {
 
 int blackhole_sm100_nvfp4_bf16_gemm(int M, int N, int K, const void* A, const void* SFA,
@@ -61,6 +110,32 @@ int blackhole_sm100_nvfp4_quantize(const void* X, int x_is_bf16, int rows, int K
                                    void* sf, float* scales, cudaStream_t stream) {
   return static_cast<int>(
       blackhole::sm100::nvfp4_quantize(X, x_is_bf16, rows, K, packed, sf, scales, stream));
+}
+
+int blackhole_sm100_nvfp4_bf16_gemm_noalloc(int M, int N, int K, const void* A, const void* SFA,
+                                            const void* B, const void* SFB, void* D, float alpha,
+                                            cudaStream_t stream) {
+  cudaError_t e = blackhole::sm100::nvfp4_check_args(M, N, K, A, SFA, B, SFB, D);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  if (M > kNoAllocMaxM) return static_cast<int>(cudaErrorInvalidValue);  // beyond the array
+  blackhole::sm100::detail::DeviceState* st = blackhole::sm100::detail::prepare_device();
+  if (!st) return static_cast<int>(cudaErrorInvalidDevice);
+  if (st->init_err != cudaSuccess) return static_cast<int>(st->init_err);
+  const int64_t need = blackhole::sm100::nvfp4_skinny_workspace_bytes(
+      st->num_sms, blackhole::sm100::nvfp4_skinny_mpad(M));
+  if (st->num_sms > kNoAllocMaxSms || need > static_cast<int64_t>(kNoAllocScratchBytes))
+    return static_cast<int>(cudaErrorInvalidValue);
+  void* scratch = nullptr;
+  e = noalloc_scratch(&scratch);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  // The array keeps whatever the previous call left; the flag words must start at zero.
+  e = cudaMemsetAsync(scratch, 0,
+                      static_cast<size_t>(blackhole::sm100::nvfp4_skinny_flag_bytes(st->num_sms)),
+                      stream);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  return static_cast<int>(blackhole::sm100::nvfp4_bf16_gemm_skinny(
+      M, N, K, A, SFA, B, SFB, D, alpha, scratch, static_cast<int64_t>(kNoAllocScratchBytes),
+      stream));
 }
 
 int blackhole_sm100_abi_version(void) { return BLACKHOLE_SM100_ABI_VERSION; }

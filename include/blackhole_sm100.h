@@ -85,6 +85,21 @@ BLACKHOLE_SM100_API int blackhole_sm100_nvfp4_quantize(const void* X, int x_is_b
                                                        void* packed, void* sf, float* scales,
                                                        cudaStream_t stream);
 
+/* Allocation-free variant of the GEMM for M <= 16 (no counterpart in the reference).
+ * For callers that may not allocate device memory when they run the GEMM (memory planned
+ * up front, no cudaMalloc synchronisation allowed on the path, or a host that passes only
+ * the input and output buffers).  It runs the skinny schedule with its scratch held in a
+ * fixed 1,313,280-byte array inside this library, sized for M <= 16 on devices with at most
+ * 160 SMs; larger M or more SMs return cudaErrorInvalidValue.  It calls no cudaMalloc or
+ * cudaFree.  The first call on each device looks up the array's device address with
+ * cudaGetSymbolAddress; make that first call before any stream capture.  Every call uses the
+ * same array and clears its flag words first (cudaMemsetAsync on `stream`), so calls that
+ * overlap on the GPU (different streams, or different host threads) race with each other. */
+BLACKHOLE_SM100_API int blackhole_sm100_nvfp4_bf16_gemm_noalloc(int M, int N, int K, const void* A,
+                                                                const void* SFA, const void* B,
+                                                                const void* SFB, void* D,
+                                                                float alpha, cudaStream_t stream);
+
 /* ABI version of the loaded library (BLACKHOLE_SM100_ABI_VERSION). */
 BLACKHOLE_SM100_API int blackhole_sm100_abi_version(void);
 
