@@ -1,0 +1,82 @@
+"""N-split of the NVFP4 GEMM across the GPUs of one node (host-side plumbing).
+
+Rank r of P owns rows [r*N/P, (r+1)*N/P) of B (the GEMM's N dimension) and the matching
+scale factors; A and its scale factors are replicated.  Each rank runs the single-GPU
+operator on (M, N/P, K) and produces an M x N/P slice of D; no GPU reads another GPU's
+memory.  An optional all-gather assembles the slices as [P][M][N/P].
+
+Because a shard is a whole number of 128-row blocks, its SFB is one contiguous byte range of
+the full SFB tensor (the 128x4 layout advances along K inside a row block, then to the next
+block), so shards are plain views: no repacking.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+from blackhole_b200 import sf_storage_bytes
+
+
+@dataclass(frozen=True)
+class Shard:
+    rank: int
+    world: int
+    row0: int        # first row of B owned by this rank
+    rows: int        # rows owned (N / world)
+    b_offset: int    # byte offset of the shard in packed B
+    b_bytes: int
+    sf_offset: int   # byte offset of the shard's scale factors in SFB
+    sf_bytes: int
+
+
+def shard(N: int, K: int, rank: int, world: int) -> Shard:
+    """Rows of B (and bytes of B / SFB) that `rank` owns in an even N-split."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("bad rank / world")
+    if N % (128 * world) != 0:
+        raise ValueError(f"N={N} must split into {world} shards of whole 128-row blocks")
+    rows = N // world
+    row0 = rank * rows
+    sf_per_shard = sf_storage_bytes(rows, K)
+    return Shard(rank, world, row0, rows, row0 * (K // 2), rows * (K // 2),
+                 rank * sf_per_shard, sf_per_shard)
+
+
+def shard_views(B, SFB, N: int, K: int, rank: int, world: int):
+    """Views of this rank's rows of packed B and of its SFB bytes (1-D byte tensors or
+    arrays, or 2-D [N, K/2] B); no copy."""
+    s = shard(N, K, rank, world)
+    if getattr(B, "ndim", 1) == 2:
+        b = B[s.row0:s.row0 + s.rows]
+    else:
+        b = B[s.b_offset:s.b_offset + s.b_bytes]
+    return b, SFB[s.sf_offset:s.sf_offset + s.sf_bytes]
+
+
+def assemble(gathered, world: int):
+    """[P][M][N/P] slices (the all-gather layout) -> row-major [M][N]."""
+    P, M, n = gathered.shape
+    assert P == world
+    if hasattr(gathered, "permute"):
+        return gathered.permute(1, 0, 2).reshape(M, P * n)
+    return gathered.transpose(1, 0, 2).reshape(M, P * n)
+
+
+def nsplit_gemm(M: int, N: int, K: int, A, SFA, B, SFB, alpha: float, rank: int, world: int,
+                gather: bool = False, group=None, stream=None):
+    """Runs this rank's slice on the current CUDA device; returns the M x N/P slice, or with
+    gather=True the assembled M x N result (NCCL all-gather through torch.distributed)."""
+    import torch
+
+    import blackhole_b200 as bh
+
+    s = shard(N, K, rank, world)
+    b, sfb = shard_views(B, SFB, N, K, rank, world)
+    D = torch.empty((M, s.rows), dtype=torch.bfloat16, device=A.device)
+    bh.nvfp4_bf16_gemm(M, s.rows, K, A, SFA, b, sfb, D, alpha, stream=stream)
+    if not gather or world == 1:
+        return D
+    import torch.distributed as dist
+
+    out = torch.empty((world, M, s.rows), dtype=torch.bfloat16, device=A.device)
+    dist.all_gather_into_tensor(out, D, group=group)
+    return assemble(out, world)

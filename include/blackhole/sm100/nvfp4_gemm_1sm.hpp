@@ -137,6 +137,7 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  pdl_launch_dependents();  // the next kernel may claim SMs as ours exit
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -163,6 +164,8 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // the previous kernel in the stream must be complete before global memory is touched
+  pdl_wait_prior_grid();
 
   if (warp == KT::ProducerWarp) {
     // ------------------------------ TMA producer ------------------------------------
@@ -396,7 +399,8 @@ inline cudaError_t launch_1sm(int M, int N, int K, const void* A, const void* SF
   p.sf_k_atoms = static_cast<int>(sf_k_atoms(K));
   p.n_blocks128 = N / 128;
   const int grid = p.num_tiles < st->num_sms ? p.num_tiles : st->num_sms;
-  nvfp4_gemm_kernel<KT><<<grid, KT::NumThreads, KT::SmemBytes, stream>>>(p);
+  e = launch_pdl(nvfp4_gemm_kernel<KT>, dim3(grid), dim3(KT::NumThreads), KT::SmemBytes, stream, p);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

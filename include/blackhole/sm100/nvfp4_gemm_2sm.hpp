@@ -132,6 +132,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  pdl_launch_dependents();  // the next kernel may claim SMs as ours exit
   const uint32_t rank = cluster_ctarank();          // 0 = leader, 1 = peer
   const int cluster = blockIdx.x >> 1;
   const int num_clusters = gridDim.x >> 1;
@@ -164,6 +165,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
   cluster_sync();  // barriers of both CTAs initialised before any cross-CTA signal
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // the previous kernel in the stream must be complete before global memory is touched
+  pdl_wait_prior_grid();
 
   if (warp == KT::ProducerWarp) {
     // ------------------------------ TMA producer (both CTAs) ------------------------
@@ -413,7 +416,9 @@ inline cudaError_t launch_2sm(int M, int N, int K, const void* A, const void* SF
     clusters = resident[dev & 63];
   }
   if (p.num_tiles < clusters) clusters = p.num_tiles;
-  nvfp4_gemm_2sm_kernel<KT><<<2 * clusters, KT::NumThreads, KT::SmemBytes, stream>>>(p);
+  e = launch_pdl(nvfp4_gemm_2sm_kernel<KT>, dim3(2 * clusters), dim3(KT::NumThreads), KT::SmemBytes,
+                 stream, p);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

@@ -83,10 +83,51 @@ inline EncodeTiledFn encode_tiled_fn() {
   return fn;
 }
 
+// Encoding a tensor map costs microseconds on the host, comparable to a decode-sized GEMM,
+// so encoded maps are kept in a small per-thread cache keyed by everything they encode
+// (kind, base address, extents, box).  A map holds no reference to the memory, so a hit
+// after the buffer was freed and another allocated at the same address is still correct.
+struct TmapKey {
+  int kind;
+  const void* base;
+  int64_t a, b;
+  uint32_t c, d;
+  bool operator==(const TmapKey& o) const {
+    return kind == o.kind && base == o.base && a == o.a && b == o.b && c == o.c && d == o.d;
+  }
+};
+
+template <class Make>
+inline cudaError_t cached_tmap(const TmapKey& key, CUtensorMap* out, Make make) {
+  struct Entry {
+    TmapKey key;
+    CUtensorMap map;
+    bool valid = false;
+  };
+  constexpr int kEntries = 16;
+  thread_local Entry cache[kEntries];
+  thread_local int next = 0;
+  for (int i = 0; i < kEntries; ++i) {
+    if (cache[i].valid && cache[i].key == key) {
+      *out = cache[i].map;
+      return cudaSuccess;
+    }
+  }
+  cudaError_t e = make(out);
+  if (e != cudaSuccess) return e;
+  Entry& slot = cache[next];
+  next = (next + 1) % kEntries;
+  slot.key = key;
+  slot.map = *out;
+  slot.valid = true;
+  return cudaSuccess;
+}
+
 // 2-D K-major byte tensor [rows][row_bytes] with a (box_rows x box_bytes) box swizzled at
 // box_bytes (128, 64 or 32).  Rows past `rows` read as zero.
-inline cudaError_t make_kmajor_tmap(CUtensorMap* m, const void* base, int64_t rows,
-                                    int64_t row_bytes, uint32_t box_rows, uint32_t box_bytes = 128) {
+inline cudaError_t make_kmajor_tmap_uncached(CUtensorMap* m, const void* base, int64_t rows,
+                                             int64_t row_bytes, uint32_t box_rows,
+                                             uint32_t box_bytes) {
   EncodeTiledFn enc = encode_tiled_fn();
   if (!enc) return cudaErrorNotSupported;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(rows)};
@@ -105,8 +146,8 @@ inline cudaError_t make_kmajor_tmap(CUtensorMap* m, const void* base, int64_t ro
 // Scale factors viewed as rows of 512-byte atoms (64 x 8 bytes): [row_blocks * k_atoms][64].
 // A box of box_atoms atoms is one (64 * box_atoms)-wide k-tile of one 128-row block; atoms
 // past the end (row blocks beyond the tensor) read as zero.
-inline cudaError_t make_sf_tmap(CUtensorMap* m, const void* base, int64_t mn, int64_t k,
-                                uint32_t box_atoms = 4) {
+inline cudaError_t make_sf_tmap_uncached(CUtensorMap* m, const void* base, int64_t mn, int64_t k,
+                                         uint32_t box_atoms) {
   EncodeTiledFn enc = encode_tiled_fn();
   if (!enc) return cudaErrorNotSupported;
   const int64_t atoms = ((mn + 127) / 128) * sf_k_atoms(k);
@@ -123,8 +164,8 @@ inline cudaError_t make_sf_tmap(CUtensorMap* m, const void* base, int64_t mn, in
 // Row-major BF16 [rows][cols] output with a (32 rows x box_cols columns) box: the store box
 // of one epilogue warp.  Parts of a box past the tensor edge are not written.
 // box_cols = 64 (128-byte rows, 128B swizzle) or 16 (32-byte rows, 32B swizzle).
-inline cudaError_t make_d_tmap(CUtensorMap* m, void* base, int64_t rows, int64_t cols,
-                               uint32_t box_cols = 64) {
+inline cudaError_t make_d_tmap_uncached(CUtensorMap* m, void* base, int64_t rows, int64_t cols,
+                                        uint32_t box_cols) {
   EncodeTiledFn enc = encode_tiled_fn();
   if (!enc) return cudaErrorNotSupported;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
@@ -138,6 +179,25 @@ inline cudaError_t make_d_tmap(CUtensorMap* m, void* base, int64_t rows, int64_t
                    CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+inline cudaError_t make_kmajor_tmap(CUtensorMap* m, const void* base, int64_t rows,
+                                    int64_t row_bytes, uint32_t box_rows, uint32_t box_bytes = 128) {
+  return cached_tmap({0, base, rows, row_bytes, box_rows, box_bytes}, m, [&](CUtensorMap* o) {
+    return make_kmajor_tmap_uncached(o, base, rows, row_bytes, box_rows, box_bytes);
+  });
+}
+inline cudaError_t make_sf_tmap(CUtensorMap* m, const void* base, int64_t mn, int64_t k,
+                                uint32_t box_atoms = 4) {
+  return cached_tmap({1, base, mn, k, box_atoms, 0}, m, [&](CUtensorMap* o) {
+    return make_sf_tmap_uncached(o, base, mn, k, box_atoms);
+  });
+}
+inline cudaError_t make_d_tmap(CUtensorMap* m, void* base, int64_t rows, int64_t cols,
+                               uint32_t box_cols = 64) {
+  return cached_tmap({2, base, rows, cols, box_cols, 0}, m, [&](CUtensorMap* o) {
+    return make_d_tmap_uncached(o, base, rows, cols, box_cols);
+  });
 }
 
 struct DeviceState {
@@ -182,6 +242,25 @@ inline cudaError_t set_smem_once(Kernel kernel, int bytes, int dev) {
       cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   done[key] = e;
   return e;
+}
+
+// Launches with programmatic stream serialization, so the kernel may start while the
+// previous kernel in the stream drains (the kernels call pdl_wait_prior_grid() before they
+// touch global memory).
+template <class Params>
+inline cudaError_t launch_pdl(void (*kernel)(Params), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, const Params& p) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 
 }  // namespace detail

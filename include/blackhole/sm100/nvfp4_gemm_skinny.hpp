@@ -181,6 +181,7 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  pdl_launch_dependents();  // the next kernel may claim SMs as ours exit
   const int c = blockIdx.x;
 
   if (threadIdx.x == 0) {
@@ -209,6 +210,8 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // the previous kernel in the stream must be complete before global memory is touched
+  pdl_wait_prior_grid();
 
   if (warp == KT::ProducerWarp) {
     // ------------------------------ TMA producer ------------------------------------
@@ -448,7 +451,9 @@ inline cudaError_t launch_skinny(int M, int N, int K, const void* A, const void*
   p.K = K;
   p.grid = grid;
   p.sf_k_atoms = static_cast<int>(sf_k_atoms(K));
-  nvfp4_gemm_skinny_kernel<KT><<<grid, KT::NumThreads, KT::SmemBytes, stream>>>(p);
+  e = launch_pdl(nvfp4_gemm_skinny_kernel<KT>, dim3(grid), dim3(KT::NumThreads), KT::SmemBytes,
+                 stream, p);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

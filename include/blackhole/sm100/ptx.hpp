@@ -22,6 +22,18 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// ---- programmatic dependent launch ---------------------------------------------------------
+// Both are no-ops unless the kernel was launched with programmatic stream serialization.
+// launch_dependents lets the next kernel in the stream be scheduled (its CTAs take SMs as
+// this kernel's CTAs exit); wait blocks until the previous kernel has completed and its
+// memory is visible, so it goes before the first read of inputs or write of outputs.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait_prior_grid() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // ---- mbarrier ---------------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
