@@ -48,6 +48,9 @@ def parse():
     ap.add_argument("--n", type=int, default=8192, help="columns per GPU")
     ap.add_argument("--k", type=int, default=8192)
     ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--case", default="all", choices=["all", "main", "decode"],
+                    help="main: only the 8192^3-class GEMM; decode: only the M=16 GEMM "
+                         "(small runs for profiler captures; the JSON line then lacks the other)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--gather", action="store_true", help="also time the NCCL all-gather (P>1)")
@@ -342,6 +345,32 @@ def reference_arm(args, world, rank):
     }
 
 
+def run_decode(args, dev, rank, world, hbm_peak, peak_src):
+    """The M=16 decode GEMM over 3 rotating weight sets, back to back."""
+    import torch
+
+    Md, Nd, Kd = 16, 28672, 8192
+    dsets = []
+    for i in range(3):
+        Ad, SFAd, scAd = make_operand(Md, Kd, 2 + 7 * i, 1.0, dev)
+        Bd, SFBd, scBd = make_operand(Nd, Kd, 2000 + rank + 7 * i, 0.02, dev)
+        dsets.append((Ad, SFAd, Bd, SFBd, float(scAd[1].item() * scBd[1].item())))
+    Dd = torch.empty((Md, Nd), dtype=torch.bfloat16, device=dev)
+    dsteps = max(30, args.steps)
+    dtot = time_gemm(Md, Nd, Kd, dsets, Dd, dsteps, args.warmup, world)
+    dms = max_over_ranks(dtot / dsteps, world)
+    nbytes = gemm_bytes(Md, Nd, Kd)
+    gbs = nbytes / (dms * 1e-3) / 1e9
+    return {"workload": f"M={Md} N={Nd} K={Kd} (BASELINE configs[2]) per GPU",
+            "value": gbs * world, "unit": "GB/s", "ms_per_step": dms,
+            "bytes_per_launch": nbytes, "roofline_frac": gbs / hbm_peak,
+            "peak": hbm_peak, "peak_source": peak_src,
+            "frac_of_spec_8tbs": gbs / SPEC_HBM_GBS, "steps": dsteps,
+            "l2": "3 rotating weight sets (396 MB > 126 MB L2), back to back",
+            "host_enqueue_us_per_launch": time_gemm.host_us_per_launch,
+            "traffic": profiled_traffic(f"gemm_{Md}x{Nd}x{Kd}")}
+
+
 # ---------------------------------------------------------------------------------------
 def main():
     args = parse()
@@ -361,6 +390,20 @@ def main():
     hbm_peak, bf16_peak, peak_src = measured_peaks()
     fp4_peak = 4.0 * bf16_peak
     M, N, K = args.m, args.n, args.k
+    if args.case == "decode":
+        with ClockSampler(torch.cuda.current_device()) as clk:
+            d = run_decode(args, dev, rank, world, hbm_peak, peak_src)
+        assert bh.device_status(torch.cuda.current_device()) == 0
+        if rank == 0:
+            print(json.dumps({"case": "decode", "decode": d, "gpu_launches": d["steps"],
+                              "clocks": clk.summary()}), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+    if args.case == "main":
+        args.no_decode = True
 
     ROT = 4
     sets = []
@@ -409,28 +452,8 @@ def main():
     }
 
     if not args.no_decode:
-        Md, Nd, Kd = 16, 28672, 8192
-        dsets = []
-        for i in range(3):
-            Ad, SFAd, scAd = make_operand(Md, Kd, 2 + 7 * i, 1.0, dev)
-            Bd, SFBd, scBd = make_operand(Nd, Kd, 2000 + rank + 7 * i, 0.02, dev)
-            dsets.append((Ad, SFAd, Bd, SFBd, float(scAd[1].item() * scBd[1].item())))
-        Dd = torch.empty((Md, Nd), dtype=torch.bfloat16, device=dev)
-        dsteps = max(30, args.steps)
-        dtot = time_gemm(Md, Nd, Kd, dsets, Dd, dsteps, args.warmup, world)
-        dms = max_over_ranks(dtot / dsteps, world)
-        nbytes = gemm_bytes(Md, Nd, Kd)
-        gbs = nbytes / (dms * 1e-3) / 1e9
-        result["decode"] = {"workload": f"M={Md} N={Nd} K={Kd} (BASELINE configs[2]) per GPU",
-                            "value": gbs * world, "unit": "GB/s", "ms_per_step": dms,
-                            "bytes_per_launch": nbytes, "roofline_frac": gbs / hbm_peak,
-                            "peak": hbm_peak, "peak_source": peak_src,
-                            "frac_of_spec_8tbs": gbs / SPEC_HBM_GBS, "steps": dsteps,
-                            "l2": "3 rotating weight sets (396 MB > 126 MB L2), back to back",
-                            "host_enqueue_us_per_launch": time_gemm.host_us_per_launch,
-                            "traffic": profiled_traffic(f"gemm_{Md}x{Nd}x{Kd}")}
-        result["gpu_launches"] += dsteps
-        del dsets, Dd
+        result["decode"] = run_decode(args, dev, rank, world, hbm_peak, peak_src)
+        result["gpu_launches"] += result["decode"]["steps"]
 
     if world > 1 and args.gather:
         import torch.distributed as dist

@@ -66,6 +66,8 @@ def load():
     L.blackhole_sm100_device_status.argtypes = [i32, ctypes.POINTER(ctypes.c_uint), i32]
     L.blackhole_sm100_nvfp4_quantize.restype = i32
     L.blackhole_sm100_nvfp4_quantize.argtypes = [vp, i32, i32, i32, vp, vp, vp, vp]
+    L.blackhole_sm100_selftest_bounded_wait.restype = i32
+    L.blackhole_sm100_selftest_bounded_wait.argtypes = [ctypes.c_uint64, vp, vp]
     L.blackhole_sm100_abi_version.restype = i32
     L.blackhole_sm100_abi_version.argtypes = []
     _lib = L
@@ -172,6 +174,15 @@ def device_status(device: int = 0, clear: bool = True) -> int:
         raise BlackholeError("blackhole_sm100_device_status", rc)
     return int(out.value)
 
+
+def selftest_bounded_wait(limit_ns: int, result, stream=None) -> None:
+    """Launches the bounded-wait self-test kernel (asynchronous): its producer warp times out
+    after `limit_ns` and sets status bit 0; its consumer warp must leave through the CTA abort
+    flag.  `result`: 4 device int64 words (completed flags of both warps, then their waits in
+    ns)."""
+    rc = load().blackhole_sm100_selftest_bounded_wait(int(limit_ns), _ptr(result), _stream(stream))
+    if rc != 0:
+        raise BlackholeError("blackhole_sm100_selftest_bounded_wait", rc)
 
 
 def nvfp4_quantize(X, rows: int, K: int, packed, sf, scales, x_is_bf16: bool = False, stream=None) -> None:

@@ -6,6 +6,7 @@
 #include <blackhole/common/sf_layout.hpp>
 #include <blackhole/sm100/nvfp4_gemm.hpp>
 #include <blackhole/sm100/nvfp4_quant.hpp>
+#include <blackhole/sm100/bounded_wait_selftest.hpp>
 
 #include <mutex>
 
@@ -136,6 +137,11 @@ int blackhole_sm100_nvfp4_bf16_gemm_noalloc(int M, int N, int K, const void* A, 
   return static_cast<int>(blackhole::sm100::nvfp4_bf16_gemm_skinny(
       M, N, K, A, SFA, B, SFB, D, alpha, scratch, static_cast<int64_t>(kNoAllocScratchBytes),
       stream));
+}
+
+int blackhole_sm100_selftest_bounded_wait(uint64_t limit_ns, uint64_t* result,
+                                          cudaStream_t stream) {
+  return static_cast<int>(blackhole::sm100::bounded_wait_selftest(limit_ns, result, stream));
 }
 
 int blackhole_sm100_abi_version(void) { return BLACKHOLE_SM100_ABI_VERSION; }

@@ -80,14 +80,14 @@ __device__ __forceinline__ uint32_t mbar_probe(uint32_t bar, uint32_t parity) {
 // the flag is raised and `code` is or-ed into *status so the host can see it.
 __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity,
                                              volatile int* abort_flag, uint32_t* status,
-                                             uint32_t code) {
+                                             uint32_t code, uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0) {
       if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > limit_ns) {
         *abort_flag = 1;
         if (status) atomicOr(status, code);
         return false;
@@ -101,7 +101,8 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity,
 // warp never splits between "done" and "abort" and no later warp-wide operation can hang.
 __device__ __forceinline__ bool wait_bounded_warp(uint32_t bar, uint32_t parity,
                                                   volatile int* abort_flag, uint32_t* status,
-                                                  uint32_t code) {
+                                                  uint32_t code,
+                                                  uint64_t limit_ns = kWaitLimitNs) {
   if (__all_sync(0xFFFFFFFFu, mbar_try_wait(bar, parity))) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
@@ -111,7 +112,7 @@ __device__ __forceinline__ bool wait_bounded_warp(uint32_t bar, uint32_t parity,
       if ((threadIdx.x & 31) == 0) {
         if (*abort_flag) {
           give_up = 1;
-        } else if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        } else if (globaltimer_ns() - t0 > limit_ns) {
           *abort_flag = 1;
           if (status) atomicOr(status, code);
           give_up = 1;

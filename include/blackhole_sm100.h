@@ -100,6 +100,15 @@ BLACKHOLE_SM100_API int blackhole_sm100_nvfp4_bf16_gemm_noalloc(int M, int N, in
                                                                 const void* SFB, void* D,
                                                                 float alpha, cudaStream_t stream);
 
+/* Self-test of the bounded-wait protocol (no counterpart in the reference): one CTA whose
+ * "producer" warp waits limit_ns on a barrier nothing arrives on, gives up, raises the CTA
+ * abort flag and sets status bit 0; its "consumer" warp, holding TMEM, must leave through
+ * the abort flag (bit 1 stays clear) and free its TMEM.  result: 4 device uint64 words
+ * (completed flags of the two warps, then their wait times in ns).  0 < limit_ns <= 2e9.
+ * Asynchronous on `stream`; read the status with blackhole_sm100_device_status. */
+BLACKHOLE_SM100_API int blackhole_sm100_selftest_bounded_wait(uint64_t limit_ns, uint64_t* result,
+                                                              cudaStream_t stream);
+
 /* ABI version of the loaded library (BLACKHOLE_SM100_ABI_VERSION). */
 BLACKHOLE_SM100_API int blackhole_sm100_abi_version(void);
 
