@@ -21,16 +21,17 @@
 // per CTA), so this entry point keeps that scratch in a fixed array of this module instead.
 //
 // The array holds what M <= 16 needs on a device with up to 160 SMs:
-//   flags    : 160 CTAs x 4 warps x 4 bytes = 2560 bytes (already a multiple of 256)
+//   flags    : 160 CTAs x 4 warps x 4 bytes + a 4-byte ticket counter, padded to 2816 bytes
 //   partials : 160 CTAs x 16 rows x 128 columns x 4 bytes = 1,310,720 bytes
-// Every GPU that loads this library holds these 1,313,280 bytes until the process exits.
+// Every GPU that loads this library holds these 1,313,536 bytes until the process exits.
 // ---------------------------------------------------------------------------------------
 namespace {
 
 constexpr int kNoAllocMaxM = 16;
 constexpr int kNoAllocMaxSms = 160;
-constexpr size_t kNoAllocScratchBytes =
-    size_t(kNoAllocMaxSms) * 16 + size_t(kNoAllocMaxSms) * kNoAllocMaxM * 128 * 4;
+constexpr size_t kNoAllocScratchBytes = static_cast<size_t>(
+    blackhole::sm100::nvfp4_skinny_workspace_bytes(kNoAllocMaxSms, kNoAllocMaxM));
+static_assert(kNoAllocScratchBytes == 1313536, "documented size of the scratch array");
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
@@ -70,7 +71,7 @@ int blackhole_sm100_nvfp4_bf16_gemm_ex(int M, int N, int K, const void* A, const
                                        const void* B, const void* SFB, void* D, float alpha,
                                        int schedule, void* workspace, int64_t workspace_bytes,
                                        cudaStream_t stream) {
-  if (schedule < 0 || schedule > 3) return static_cast<int>(cudaErrorInvalidValue);
+  if (schedule < 0 || schedule > 4) return static_cast<int>(cudaErrorInvalidValue);
   return static_cast<int>(blackhole::sm100::nvfp4_bf16_gemm_ex(
       M, N, K, A, SFA, B, SFB, D, alpha, static_cast<blackhole::sm100::Nvfp4Schedule>(schedule),
       workspace, workspace_bytes, stream));

@@ -17,7 +17,9 @@
 // Schedules (chosen by shape):
 //   * M <= 128 : skinny schedule (nvfp4_gemm_skinny.hpp) -- swap-AB, stream-K over all SMs,
 //                HBM-bound; needs a small FP32 workspace (allocated here per device and
-//                stream on first use, or passed by the caller: nvfp4_bf16_gemm_ex);
+//                stream on first use, or passed by the caller: nvfp4_bf16_gemm_ex).  It warms
+//                L2 with its first B / SFB tiles while the previous kernel in the stream is
+//                finishing (a prefetch only: results are those of plain stream order);
 //   * M > 128  : one-SM schedule (nvfp4_gemm_1sm.hpp) -- 128 x 256 tiles, tensor-bound;
 //   * the two-SM schedule (nvfp4_gemm_2sm.hpp, 256 x 256 tiles per CTA pair) is available
 //     explicitly (on B200 it measured slower than the one-SM schedule at 8192^3).
@@ -49,7 +51,9 @@
 
 namespace blackhole::sm100 {
 
-enum class Nvfp4Schedule : int { kAuto = 0, kOneSm = 1, kTwoSm = 2, kSkinny = 3 };
+// kSkinnyNoPrefetch is the skinny schedule without the L2 prefetch of B / SFB that it issues
+// while the previous kernel in the stream is finishing (same results; for measurement).
+enum class Nvfp4Schedule : int { kAuto = 0, kOneSm = 1, kTwoSm = 2, kSkinny = 3, kSkinnyNoPrefetch = 4 };
 
 #if defined(__CUDACC__)
 
@@ -108,7 +112,8 @@ inline cudaError_t nvfp4_bf16_gemm_ex(int M, int N, int K, void const* A, void c
       return detail::launch_1sm<Nvfp4GemmTraits>(M, N, K, A, SFA, B, SFB, D, alpha, st, dev, stream);
     case Nvfp4Schedule::kTwoSm:
       return detail::launch_2sm<Nvfp4Gemm2SmTraits>(M, N, K, A, SFA, B, SFB, D, alpha, st, dev, stream);
-    case Nvfp4Schedule::kSkinny: {
+    case Nvfp4Schedule::kSkinny:
+    case Nvfp4Schedule::kSkinnyNoPrefetch: {
       if (M > 128) return cudaErrorInvalidValue;
       const int64_t need = nvfp4_skinny_workspace_bytes(st->num_sms, nvfp4_skinny_mpad(M));
       if (!workspace) {
@@ -117,7 +122,7 @@ inline cudaError_t nvfp4_bf16_gemm_ex(int M, int N, int K, void const* A, void c
         workspace_bytes = need;
       }
       return nvfp4_bf16_gemm_skinny(M, N, K, A, SFA, B, SFB, D, alpha, workspace, workspace_bytes,
-                                    stream);
+                                    stream, 1 << 30, schedule == Nvfp4Schedule::kSkinny);
     }
     default:
       return cudaErrorInvalidValue;

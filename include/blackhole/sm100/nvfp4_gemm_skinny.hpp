@@ -46,6 +46,11 @@ struct Nvfp4SkinnyTraits {
   static constexpr int SFBytes = KSteps * 512;              // 2 KB per operand
   static constexpr int StageBytes = WBytes + XBytes + 2 * SFBytes;
   static constexpr int Stages = (MPAD <= 32) ? 9 : (MPAD == 64 ? 8 : 6);
+  // k-tiles of B prefetched into L2 before the dependency wait (beyond the smem stages)
+  static constexpr int L2PrefetchKTiles = 20;
+  // ranges by ticket: the first CTA to start gets (1 + s) x, the last (1 - s) x the mean
+  // work, s = RangeSkew / 64
+  static constexpr int RangeSkew = 6;
 
   static constexpr int NumWarps = 6;                        // TMA, MMA, 4 x epilogue
   static constexpr int NumThreads = NumWarps * 32;
@@ -65,13 +70,14 @@ struct Nvfp4SkinnyTraits {
 };
 
 // Workspace layout: flag words first, at a fixed place for the device (4 per possible CTA,
-// padded to 256 bytes), then the FP32 partials.  Keeping the flags at a fixed offset means a
-// workspace shared by calls of different M never sees partial data where a flag should be.
-inline int64_t nvfp4_skinny_flag_bytes(int num_sms) {
-  return (int64_t(num_sms) * 16 + 255) / 256 * 256;
+// then the ticket counter, padded to 256 bytes), then the FP32 partials.  Keeping the flags at
+// a fixed offset means a workspace shared by calls of different M never sees partial data
+// where a flag should be.
+constexpr int64_t nvfp4_skinny_flag_bytes(int num_sms) {
+  return (int64_t(num_sms) * 16 + 16 + 255) / 256 * 256;
 }
 // Bytes of workspace the skinny schedule needs on a device with num_sms SMs at width mpad.
-inline int64_t nvfp4_skinny_workspace_bytes(int num_sms, int mpad) {
+constexpr int64_t nvfp4_skinny_workspace_bytes(int num_sms, int mpad) {
   return nvfp4_skinny_flag_bytes(num_sms) + int64_t(num_sms) * mpad * 128 * 4;
 }
 
@@ -87,19 +93,29 @@ struct Nvfp4SkinnyParams {
   uint16_t* d;
   float* ws;            // [grid][MPAD][128] partials
   uint32_t* flags;      // [grid][4]: one per epilogue warp
+  uint32_t* ticket;     // entry counter: CTAs take ranges in the order they start
   uint32_t* status;
   float alpha;
   int M, N, K;
   int kt_per_rb;        // K / 256
   int64_t units;        // N/128 * K/256
   int grid;
+  int skew;             // range of ticket t shrinks linearly: density (1 + s - 2 s t / grid), s = skew/64
   int sf_k_atoms;
+  int l2_pf;            // k-tiles of B / SFB prefetched into L2 before the previous kernel completes
 };
 
 namespace skinny_detail {
 
-__device__ __forceinline__ int64_t range_start(const Nvfp4SkinnyParams& p, int c) {
-  return int64_t(c) * p.units / p.grid;
+// First unit of the range of ticket t.  Ranges shrink linearly with the ticket: CTAs that
+// start late (on SMs whose previous CTA finished late, or with less time to prefetch before
+// the previous kernel completes) get less work.  Monotone, range_start(grid) == units; the
+// launcher keeps every range non-empty and the products inside 63 bits.
+__device__ __forceinline__ int64_t range_start(const Nvfp4SkinnyParams& p, int t) {
+  const int64_t g = p.grid;
+  if (p.skew == 0) return int64_t(t) * p.units / g;
+  const int64_t num = (64 + p.skew) * int64_t(t) * g - p.skew * int64_t(t) * t;
+  return p.units * num / (64 * g * g);
 }
 
 // One row-block segment of a CTA's range, visited from the end of the range backwards.
@@ -179,12 +195,21 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
       reinterpret_cast<uint32_t*>(base_ptr + (bars - base) + 8 * (2 * S + 5));
   volatile int* const abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
+  volatile uint32_t* const ticket_slot = reinterpret_cast<volatile uint32_t*>(tmem_slot + 2);
+
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  pdl_launch_dependents();  // the next kernel may claim SMs as ours exit
-  const int c = blockIdx.x;
 
   if (threadIdx.x == 0) {
+    // Ranges go to CTAs in the order they start.  The taker of the last ticket resets the
+    // counter for the next launch; that launch starts taking tickets only after every CTA of
+    // this one has passed pdl_launch_dependents below, i.e. after the reset.
+    const uint32_t t = atomicAdd(p.ticket, 1u);
+    if (t == uint32_t(p.grid) - 1u) {
+      atomicExch(p.ticket, 0u);
+      __threadfence();
+    }
+    *ticket_slot = t;
     for (int s = 0; s < S; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
@@ -210,14 +235,34 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // the previous kernel in the stream must be complete before global memory is touched
-  pdl_wait_prior_grid();
+  const int c = static_cast<int>(*ticket_slot);
+  pdl_launch_dependents();  // the next kernel may claim SMs as ours exit
+  // The previous kernel in the stream must be complete before any operand or the workspace is
+  // read or written; the producer first issues L2 prefetches of B / SFB.
+  if (warp != KT::ProducerWarp) pdl_wait_prior_grid();
 
   if (warp == KT::ProducerWarp) {
     // ------------------------------ TMA producer ------------------------------------
     if (lane == 0) {
       const uint64_t pol_w = l2_policy_evict_first();   // B is streamed exactly once
       const uint64_t pol_x = l2_policy_evict_last();    // A is re-read by every CTA
+      // Before the previous kernel in the stream has completed, only L2 prefetches of this
+      // CTA's first l2_pf k-tiles of B / SFB are issued: HBM keeps streaming across the kernel
+      // boundary, and since L2 is the point of coherence a prefetch can never make a later
+      // load see stale data, whatever the previous kernel writes.
+      if (p.l2_pf > 0) {
+        SegmentWalk w0 = walk(p, c);
+        Segment s0;
+        int n = 0;
+        while (n < p.l2_pf && w0.next(s0)) {
+          const uint8_t* sfw_rb = p.sfw + int64_t(s0.rb) * p.sf_k_atoms * 512;
+          for (int kt = s0.kt0; kt < s0.kt1 && n < p.l2_pf; ++kt, ++n) {
+            tma_prefetch_l2_2d(&p.tmap_w, kt * KT::RowBytes, s0.rb * KT::TileW);
+            bulk_prefetch_l2(sfw_rb + int64_t(kt) * KT::KSteps * 512, KT::SFBytes);
+          }
+        }
+      }
+      pdl_wait_prior_grid();
       int stage = 0;
       uint32_t phase = 0;
       int64_t issued = 0;
@@ -232,12 +277,13 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
             break;
           }
           const uint32_t fb = full_bar(stage);
-          mbar_arrive_expect_tx(fb, KT::StageBytes);
-          tma_load_2d(st_w(stage), &p.tmap_w, fb, kt * KT::RowBytes, sg.rb * KT::TileW, pol_w);
-          tma_load_2d(st_x(stage), &p.tmap_x, fb, kt * KT::RowBytes, 0, pol_x);
           const int64_t k_off = int64_t(kt) * KT::KSteps * 512;
-          bulk_load(st_sfw(stage), sfw_rb + k_off, KT::SFBytes, fb, pol_w);
+          mbar_arrive_expect_tx(fb, KT::StageBytes);
+          // A (small, L2-resident) ahead of B in the copy engine's queue
+          tma_load_2d(st_x(stage), &p.tmap_x, fb, kt * KT::RowBytes, 0, pol_x);
           bulk_load(st_sfx(stage), p.sfx + k_off, KT::SFBytes, fb, pol_x);
+          tma_load_2d(st_w(stage), &p.tmap_w, fb, kt * KT::RowBytes, sg.rb * KT::TileW, pol_w);
+          bulk_load(st_sfw(stage), sfw_rb + k_off, KT::SFBytes, fb, pol_w);
           ++issued;
           if (++stage == S) {
             stage = 0;
@@ -324,11 +370,52 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
     // ------------------------------ epilogue ----------------------------------------
     const int q = warp & 3;
     const int n_local = 32 * q + lane;                            // row of the B block
+    // Adds the FP32 partials parked by the earlier CTAs sharing row block sg.rb (in a fixed
+    // order: deterministic) into v; false if a bounded wait gave up.
+    auto add_partials = [&](const Segment& sg, float (&v)[MPAD]) -> bool {
+      const int64_t rb0 = int64_t(sg.rb) * p.kt_per_rb;
+      for (int cc = c - 1; cc >= 0 && range_start(p, cc + 1) > rb0; --cc) {
+        uint32_t* flag = p.flags + 4 * cc + q;
+        int ready = 1;
+        if (lane == 0) {
+          const uint64_t t0 = globaltimer_ns();
+          while (ld_acquire(flag) == 0u) {
+            if (*abort_flag) { ready = 0; break; }
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+              *abort_flag = 1;
+              if (p.status) atomicOr(p.status, kStatusEpilogueTimeout);
+              ready = 0;
+              break;
+            }
+          }
+        }
+        ready = __shfl_sync(0xFFFFFFFFu, ready, 0);
+        if (!ready) return false;
+        (void)ld_acquire(flag);
+        const float* src = p.ws + (int64_t(cc) * MPAD) * 128 + n_local;
+#pragma unroll
+        for (int m = 0; m < MPAD; ++m)
+          if (m < p.M) v[m] += __ldcg(src + m * 128);
+        __syncwarp();
+        if (lane == 0) st_release(flag, 0u);
+      }
+      return true;
+    };
+    // For narrow MPAD the partials of a finished row block are fetched before its
+    // accumulator is ready, so that their latency is off the critical path.
+    constexpr bool kEarlyPartials = MPAD <= 32;
     int acc = 0;
     uint32_t acc_phase = 0;
     SegmentWalk w = walk(p, c);
     Segment sg;
     while (w.next(sg)) {
+      const bool finisher = sg.kt1 == p.kt_per_rb;
+      float part[kEarlyPartials ? MPAD : 1];
+      if constexpr (kEarlyPartials) {
+#pragma unroll
+        for (int m = 0; m < MPAD; ++m) part[m] = 0.f;
+        if (finisher && sg.kt0 > 0 && !add_partials(sg, part)) break;
+      }
       if (!wait_bounded_warp(acc_full(acc), acc_phase, abort_flag, p.status, kStatusEpilogueTimeout))
         break;
       tc_fence_after();
@@ -356,7 +443,7 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
       }
 
       const int n = sg.rb * 128 + n_local;
-      if (sg.kt1 != p.kt_per_rb) {
+      if (!finisher) {
         // Partial of a row block finished by a later CTA: park it, then raise this warp's flag.
         float* dst = p.ws + (int64_t(c) * MPAD) * 128 + n_local;
 #pragma unroll
@@ -367,36 +454,11 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
         if (lane == 0) st_release(p.flags + 4 * c + q, 1u);
         continue;
       }
-      if (sg.kt0 > 0) {
-        // Finisher: add the partials of the earlier CTAs that share this row block, in order.
-        const int64_t rb0 = int64_t(sg.rb) * p.kt_per_rb;
-        bool ok = true;
-        for (int cc = c - 1; cc >= 0 && range_start(p, cc + 1) > rb0; --cc) {
-          uint32_t* flag = p.flags + 4 * cc + q;
-          int ready = 1;
-          if (lane == 0) {
-            const uint64_t t0 = globaltimer_ns();
-            while (ld_acquire(flag) == 0u) {
-              if (*abort_flag) { ready = 0; break; }
-              if (globaltimer_ns() - t0 > kWaitLimitNs) {
-                *abort_flag = 1;
-                if (p.status) atomicOr(p.status, kStatusEpilogueTimeout);
-                ready = 0;
-                break;
-              }
-            }
-          }
-          ready = __shfl_sync(0xFFFFFFFFu, ready, 0);
-          if (!ready) { ok = false; break; }
-          (void)ld_acquire(flag);
-          const float* src = p.ws + (int64_t(cc) * MPAD) * 128 + n_local;
+      if constexpr (kEarlyPartials) {
 #pragma unroll
-          for (int m = 0; m < MPAD; ++m)
-            if (m < p.M) v[m] += __ldcg(src + m * 128);
-          __syncwarp();
-          if (lane == 0) st_release(flag, 0u);
-        }
-        if (!ok) break;
+        for (int m = 0; m < MPAD; ++m) v[m] += part[m];
+      } else {
+        if (sg.kt0 > 0 && !add_partials(sg, v)) break;
       }
       const float a = p.alpha;
 #pragma unroll
@@ -423,7 +485,9 @@ namespace detail {
 template <class KT>
 inline cudaError_t launch_skinny(int M, int N, int K, const void* A, const void* SFA, const void* B,
                                  const void* SFB, void* D, float alpha, void* ws, int64_t ws_bytes,
-                                 int grid_cap, DeviceState* st, cudaStream_t stream) {
+                                 int grid_cap, bool prefetch, DeviceState* st, cudaStream_t stream,
+                                 int l2_prefetch_ktiles = KT::L2PrefetchKTiles,
+                                 int skew = KT::RangeSkew) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -443,6 +507,7 @@ inline cudaError_t launch_skinny(int M, int N, int K, const void* A, const void*
   p.sfx = static_cast<const uint8_t*>(SFA);
   p.d = static_cast<uint16_t*>(D);
   p.flags = static_cast<uint32_t*>(ws);
+  p.ticket = p.flags + 4 * st->num_sms;
   p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + nvfp4_skinny_flag_bytes(st->num_sms));
   p.status = st->status;
   p.alpha = alpha;
@@ -450,7 +515,13 @@ inline cudaError_t launch_skinny(int M, int N, int K, const void* A, const void*
   p.N = N;
   p.K = K;
   p.grid = grid;
+  // skew only where every range keeps >= 2 units and range_start cannot overflow
+  p.skew = (skew > 0 && skew < 64 && p.units * (64 - skew) >= int64_t(2) * 64 * grid &&
+            p.units < (int64_t(1) << 62) / (128 * int64_t(grid) * grid))
+               ? skew
+               : 0;
   p.sf_k_atoms = static_cast<int>(sf_k_atoms(K));
+  p.l2_pf = prefetch ? l2_prefetch_ktiles : 0;
   e = launch_pdl(nvfp4_gemm_skinny_kernel<KT>, dim3(grid), dim3(KT::NumThreads), KT::SmemBytes,
                  stream, p);
   if (e != cudaSuccess) return e;
@@ -462,10 +533,16 @@ inline cudaError_t launch_skinny(int M, int N, int K, const void* A, const void*
 // Skinny-M GEMM with a caller-provided workspace of at least
 // nvfp4_skinny_workspace_bytes(num_SMs, nvfp4_skinny_mpad(M)) bytes, zero-filled before its
 // first use (the flag words must start at 0; every launch leaves them at 0).  M in [1, 128].
+//
+// With prefetch the kernel, launched as a programmatic dependent of the previous kernel in
+// the stream, issues L2 prefetches of the first B / SFB tiles of its range while that kernel
+// is finishing; every load, store and workspace access still waits for its completion, so
+// the results are those of plain stream order either way.
 inline cudaError_t nvfp4_bf16_gemm_skinny(int M, int N, int K, void const* A, void const* SFA,
                                           void const* B, void const* SFB, void* D, float alpha,
                                           void* workspace, int64_t workspace_bytes,
-                                          cudaStream_t stream = nullptr, int grid_cap = 1 << 30) {
+                                          cudaStream_t stream = nullptr, int grid_cap = 1 << 30,
+                                          bool prefetch = true) {
   cudaError_t e = nvfp4_check_args(M, N, K, A, SFA, B, SFB, D);
   if (e != cudaSuccess) return e;
   if (M > 128 || !workspace || (reinterpret_cast<uintptr_t>(workspace) & 15u))
@@ -476,16 +553,16 @@ inline cudaError_t nvfp4_bf16_gemm_skinny(int M, int N, int K, void const* A, vo
   switch (nvfp4_skinny_mpad(M)) {
     case 16:
       return detail::launch_skinny<Nvfp4SkinnyTraits<16>>(M, N, K, A, SFA, B, SFB, D, alpha, workspace,
-                                                           workspace_bytes, grid_cap, st, stream);
+                                                           workspace_bytes, grid_cap, prefetch, st, stream);
     case 32:
       return detail::launch_skinny<Nvfp4SkinnyTraits<32>>(M, N, K, A, SFA, B, SFB, D, alpha, workspace,
-                                                           workspace_bytes, grid_cap, st, stream);
+                                                           workspace_bytes, grid_cap, prefetch, st, stream);
     case 64:
       return detail::launch_skinny<Nvfp4SkinnyTraits<64>>(M, N, K, A, SFA, B, SFB, D, alpha, workspace,
-                                                           workspace_bytes, grid_cap, st, stream);
+                                                           workspace_bytes, grid_cap, prefetch, st, stream);
     default:
       return detail::launch_skinny<Nvfp4SkinnyTraits<128>>(M, N, K, A, SFA, B, SFB, D, alpha, workspace,
-                                                            workspace_bytes, grid_cap, st, stream);
+                                                            workspace_bytes, grid_cap, prefetch, st, stream);
   }
 }
 

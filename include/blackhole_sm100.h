@@ -37,14 +37,18 @@ extern "C" {
  * Shapes: M >= 1, N % 128 == 0, K % 256 == 0 (the reference also needs M % 128 == 0).
  * SFA/SFB must span blackhole_sm100_sf_storage_bytes(M|N, K) bytes (rows padded to 128).
  * Pointers must be 16-byte aligned.  Errors: cudaErrorInvalidValue for a bad shape,
- * null or misaligned pointer; otherwise the launch status, as in nvfp4_gemm.hpp:594-636. */
+ * null or misaligned pointer; otherwise the launch status, as in nvfp4_gemm.hpp:594-636.
+ * Stream-ordered.  The kernels are launched as programmatic dependents of the previous kernel
+ * in the stream: they set up while it finishes, and for M <= 128 also prefetch their first B /
+ * SFB tiles into L2 (a cache hint only), but read and write nothing before it completes. */
 BLACKHOLE_SM100_API int blackhole_sm100_nvfp4_bf16_gemm(int M, int N, int K, const void* A, const void* SFA,
                                     const void* B, const void* SFB, void* D, float alpha,
                                     cudaStream_t stream);
 
 /* Same GEMM with an explicit schedule and workspace (no counterpart in the reference, which
  * has a single schedule).  schedule: 0 = by shape (as above), 1 = one-SM 128x256 tiles,
- * 2 = two-SM 256x256 tiles (cta_group::2), 3 = skinny-M stream-K (M <= 128).
+ * 2 = two-SM 256x256 tiles (cta_group::2), 3 = skinny-M stream-K (M <= 128),
+ * 4 = skinny-M stream-K without the early L2 prefetch (same results).
  * workspace: device memory for the skinny schedule, at least
  * blackhole_sm100_workspace_bytes(M, N, K) bytes, zero-filled before its first use and left
  * zeroed by every call; NULL selects a library-owned buffer per (device, stream), allocated
@@ -89,7 +93,7 @@ BLACKHOLE_SM100_API int blackhole_sm100_nvfp4_quantize(const void* X, int x_is_b
  * For callers that may not allocate device memory when they run the GEMM (memory planned
  * up front, no cudaMalloc synchronisation allowed on the path, or a host that passes only
  * the input and output buffers).  It runs the skinny schedule with its scratch held in a
- * fixed 1,313,280-byte array inside this library, sized for M <= 16 on devices with at most
+ * fixed 1,313,536-byte array inside this library, sized for M <= 16 on devices with at most
  * 160 SMs; larger M or more SMs return cudaErrorInvalidValue.  It calls no cudaMalloc or
  * cudaFree.  The first call on each device looks up the array's device address with
  * cudaGetSymbolAddress; make that first call before any stream capture.  Every call uses the
