@@ -20,9 +20,11 @@
 //                stream on first use, or passed by the caller: nvfp4_bf16_gemm_ex).  It warms
 //                L2 with its first B / SFB tiles while the previous kernel in the stream is
 //                finishing (a prefetch only: results are those of plain stream order);
-//   * M > 128  : one-SM schedule (nvfp4_gemm_1sm.hpp) -- 128 x 256 tiles, tensor-bound;
-//   * the two-SM schedule (nvfp4_gemm_2sm.hpp, 256 x 256 tiles per CTA pair) is available
-//     explicitly (on B200 it measured slower than the one-SM schedule at 8192^3).
+//   * 128 < M <= 256 : one-SM schedule (nvfp4_gemm_1sm.hpp) -- 128 x 256 tiles;
+//   * M > 256  : two-SM schedule (nvfp4_gemm_2sm.hpp) -- 256 x 256 tiles per CTA pair
+//                (cta_group::2): a third less operand traffic into each SM than the one-SM
+//                tile, which on B200 is what limits the tensor pipe once the kernel is power
+//                capped (measured at 8192^3 with N(0,1) data: 220.8 us vs 226.5 us per launch).
 //
 // Shapes: M >= 1, N % 128 == 0, K % 256 == 0.  The reference additionally requires
 // M % 128 == 0 (nvfp4_gemm.hpp:594).  Every mbarrier wait in the kernels is bounded: a
@@ -106,7 +108,9 @@ inline cudaError_t nvfp4_bf16_gemm_ex(int M, int N, int K, void const* A, void c
   e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (schedule == Nvfp4Schedule::kAuto)
-    schedule = M <= 128 ? Nvfp4Schedule::kSkinny : Nvfp4Schedule::kOneSm;
+    schedule = M <= 128   ? Nvfp4Schedule::kSkinny
+               : M <= 256 ? Nvfp4Schedule::kOneSm
+                          : Nvfp4Schedule::kTwoSm;
   switch (schedule) {
     case Nvfp4Schedule::kOneSm:
       return detail::launch_1sm<Nvfp4GemmTraits>(M, N, K, A, SFA, B, SFB, D, alpha, st, dev, stream);
