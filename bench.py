@@ -54,6 +54,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--gather", action="store_true", help="also time the NCCL all-gather (P>1)")
+    ap.add_argument("--no-library", action="store_true",
+                    help="skip the cuBLASLt NVFP4 comparison leg (torch._scaled_mm, same operands)")
     ap.add_argument("--schedule", default="auto", choices=["auto", "1sm", "2sm"],
                     help="GEMM schedule for the main workload (auto: one-SM for M > 128)")
     return ap.parse_args()
@@ -345,6 +347,36 @@ def reference_arm(args, world, rank):
     }
 
 
+def library_baseline(M, N, K, sets, steps, warmup, world):
+    """The same GEMM through NVIDIA's library (cuBLASLt block-scaled NVFP4 kernel, reached via
+    torch._scaled_mm) on the same operands, timed the same way: a comparison, not our path.
+    The 128x4 scale-factor layout of this library is the one cuBLASLt expects."""
+    import torch
+
+    def launch(A, SFA, B, SFB, alpha):
+        torch._scaled_mm(A.view(torch.float4_e2m1fn_x2).view(M, K // 2),
+                         B.view(torch.float4_e2m1fn_x2).view(N, K // 2).t(),
+                         SFA.view(torch.float8_e4m3fn), SFB.view(torch.float8_e4m3fn),
+                         out_dtype=torch.bfloat16)
+
+    for i in range(warmup):
+        launch(*sets[i % len(sets)])
+    barrier(world)
+    time.sleep(1.0)  # let the power limiter settle as before our own timed region
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        for i in range(steps):
+            launch(*sets[i % len(sets)])
+        e.record()
+        barrier(world)
+    ms = max_over_ranks(s.elapsed_time(e) / steps, world)
+    return {"impl": "cuBLASLt NVFP4 block-scaled GEMM via torch._scaled_mm (comparison only)",
+            "tflops": 2.0 * M * N * K * world / (ms * 1e-3) / 1e12, "ms_per_step": ms,
+            "steps": steps, "clocks": clk.summary()}
+
+
 def run_decode(args, dev, rank, world, hbm_peak, peak_src):
     """The M=16 decode GEMM over 3 rotating weight sets, back to back."""
     import torch
@@ -484,6 +516,15 @@ def main():
         result["gpu_launches"] += esteps + 1
 
     result["clocks"] = clk.summary()
+
+    # last, so that it cannot disturb our own legs (the GPU is left hot and power capped)
+    if not args.no_library:
+        try:
+            lib = library_baseline(M, N, K, sets, args.steps, args.warmup, world)
+            lib["ours_over_library"] = value / lib["tflops"]
+            result["library_baseline"] = lib
+        except Exception as exc:  # an older torch without FP4 _scaled_mm
+            result["library_baseline"] = {"unavailable": repr(exc)[:200]}
 
     if rank == 0 and world == 1 and not args.no_cpu:
         hA = A.cpu().numpy().reshape(-1)
