@@ -22,7 +22,10 @@
 //
 // Per SM and per 128-clock MMA this moves 38 KB into shared memory instead of the 54 KB a
 // one-SM 128 x 256 tile needs, and B crosses L2 -> SM once per pair instead of twice.
-// Scale factors are fetched through tensor maps so ragged M / N edges read zeros.
+// Scale factors are fetched through 3-D tensor maps ([row block][k-tile][2 KB]) as whole 2 KB
+// rows, one request per operand and k-tile (ragged M / N edges read zeros): on B200 every
+// scale-factor request in flight slows the tensor pipe far beyond its bytes (as four 512-byte
+// rows per block they cost ~20% of the mainloop; as 2 KB rows ~10%).
 // =====================================================================================
 
 #include <blackhole/sm100/nvfp4_gemm_common.hpp>
@@ -69,6 +72,7 @@ struct Nvfp4Gemm2SmTraitsT {
   static constexpr int RasterGroupM = 8;         // in 256-row tiles
 
   static_assert(SmemBytes <= arch_traits<Arch::kSm100>::max_smem_per_cta, "smem budget");
+  static_assert(TileK == 256, "scale factors are fetched as one 2 KB row per block and k-tile");
 };
 using Nvfp4Gemm2SmTraits = Nvfp4Gemm2SmTraitsT<256, 5>;
 
@@ -77,8 +81,8 @@ using Nvfp4Gemm2SmTraits = Nvfp4Gemm2SmTraitsT<256, 5>;
 struct Nvfp4Gemm2SmParams {
   CUtensorMap tmap_a;     // A  [M][K/2] bytes, box 128 x 128 B, 128B swizzle
   CUtensorMap tmap_b;     // B  [N][K/2] bytes, box 128 x 128 B, 128B swizzle
-  CUtensorMap tmap_sfa;   // SFA atoms [M/128 * K/64][512 B], box 4 atoms
-  CUtensorMap tmap_sfb;   // SFB atoms [N/128 * K/64][512 B], box 4 atoms
+  CUtensorMap tmap_sfa;   // SFA [M/128][K/256][2048 B], box one block x one k-tile
+  CUtensorMap tmap_sfb;   // SFB [N/128][K/256][2048 B], box two blocks x one k-tile
   CUtensorMap tmap_d;     // D  [M][N] bf16, box 32 rows x 64 columns, 128B swizzle
   uint32_t* status;
   float alpha;
@@ -181,9 +185,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
         detail::tile_coords_2sm(tile, p, m_blk, n_blk);
         const int a_row = m_blk * KT::TileM + int(rank) * KT::CtaM;
         const int b_row = n_blk * KT::TileN + int(rank) * KT::CtaN;
-        const int sfa_atom = (m_blk * 2 + int(rank)) * p.sf_k_atoms;
-        const int sfb_atom0 = (n_blk * 2) * p.sf_k_atoms;
-        const int sfb_atom1 = sfb_atom0 + p.sf_k_atoms;
+        const int sfa_blk = m_blk * 2 + int(rank);
+        const int sfb_blk = n_blk * 2;
         for (int kt = 0; kt < p.k_tiles; ++kt) {
           if (!wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, p.status, kStatusLoadTimeout)) {
             ok = false;
@@ -193,10 +196,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
           if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), 2u * KT::StageBytes);
           tma_load_2d_pair(sA + stage * KT::ABytes, &p.tmap_a, lb, kt * KT::RowBytes, a_row, pol);
           tma_load_2d_pair(sB + stage * KT::BBytes, &p.tmap_b, lb, kt * KT::RowBytes, b_row, pol);
-          tma_load_2d_pair(sSFA + stage * KT::SFABytes, &p.tmap_sfa, lb, 0, sfa_atom + KT::KSteps * kt, pol);
-          tma_load_2d_pair(sSFB + stage * KT::SFBBytes, &p.tmap_sfb, lb, 0, sfb_atom0 + KT::KSteps * kt, pol);
-          tma_load_2d_pair(sSFB + stage * KT::SFBBytes + KT::SFBBytes / 2, &p.tmap_sfb, lb, 0,
-                           sfb_atom1 + KT::KSteps * kt, pol);
+          // one request per operand: SFA as one 2 KB row, SFB as the pair's two 2 KB rows
+          tma_load_3d_pair(sSFA + stage * KT::SFABytes, &p.tmap_sfa, lb, 0, kt, sfa_blk, pol);
+          tma_load_3d_pair(sSFB + stage * KT::SFBBytes, &p.tmap_sfb, lb, 0, kt, sfb_blk, pol);
           ++issued;
           if (++stage == S) {
             stage = 0;
@@ -376,9 +378,9 @@ inline cudaError_t launch_2sm(int M, int N, int K, const void* A, const void* SF
   if (e != cudaSuccess) return e;
   e = make_kmajor_tmap(&p.tmap_b, B, N, K / 2, KT::CtaN, KT::RowBytes);
   if (e != cudaSuccess) return e;
-  e = make_sf_tmap(&p.tmap_sfa, SFA, M, K, KT::KSteps);
+  e = make_sf_tmap_ktile(&p.tmap_sfa, SFA, M, K, 1, 1);
   if (e != cudaSuccess) return e;
-  e = make_sf_tmap(&p.tmap_sfb, SFB, N, K, KT::KSteps);
+  e = make_sf_tmap_ktile(&p.tmap_sfb, SFB, N, K, 2, 1);
   if (e != cudaSuccess) return e;
   e = make_d_tmap(&p.tmap_d, D, M, N);
   if (e != cudaSuccess) return e;

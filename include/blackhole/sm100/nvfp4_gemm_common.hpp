@@ -161,6 +161,29 @@ inline cudaError_t make_sf_tmap_uncached(CUtensorMap* m, const void* base, int64
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+// Scale factors of one operand as a 3-D tensor [row blocks][k-tiles][2048 B]: the 4 atoms of
+// one 128-row block and one 256-wide k-tile are 2 KB contiguous.  A box of {2048 B, ktiles,
+// blocks} fetches `ktiles` k-tiles of `blocks` consecutive row blocks in one request, as
+// 2 KB rows, landing as [block][k-tile][2048 B]; parts past the edge read zeros.  (Measured
+// on B200: every scale-factor request in flight slows the two-SM schedule's tensor pipe, far
+// beyond its bytes, so they are made few and long.)
+inline cudaError_t make_sf_tmap_ktile_uncached(CUtensorMap* m, const void* base, int64_t mn,
+                                               int64_t k, uint32_t blocks, uint32_t ktiles) {
+  EncodeTiledFn enc = encode_tiled_fn();
+  if (!enc) return cudaErrorNotSupported;
+  const int64_t k_atoms = sf_k_atoms(k);
+  if (k_atoms % 4 != 0) return cudaErrorInvalidValue;
+  cuuint64_t dims[3] = {256u, static_cast<cuuint64_t>(k_atoms / 4),
+                        static_cast<cuuint64_t>((mn + 127) / 128)};
+  cuuint64_t strides[2] = {2048u, static_cast<cuuint64_t>(k_atoms * 512)};
+  cuuint32_t box[3] = {256u, ktiles, blocks};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<void*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 // Row-major BF16 [rows][cols] output with a (32 rows x box_cols columns) box: the store box
 // of one epilogue warp.  Parts of a box past the tensor edge are not written.
 // box_cols = 64 (128-byte rows, 128B swizzle) or 16 (32-byte rows, 32B swizzle).
@@ -191,6 +214,12 @@ inline cudaError_t make_sf_tmap(CUtensorMap* m, const void* base, int64_t mn, in
                                 uint32_t box_atoms = 4) {
   return cached_tmap({1, base, mn, k, box_atoms, 0}, m, [&](CUtensorMap* o) {
     return make_sf_tmap_uncached(o, base, mn, k, box_atoms);
+  });
+}
+inline cudaError_t make_sf_tmap_ktile(CUtensorMap* m, const void* base, int64_t mn, int64_t k,
+                                      uint32_t blocks, uint32_t ktiles) {
+  return cached_tmap({3, base, mn, k, blocks, ktiles}, m, [&](CUtensorMap* o) {
+    return make_sf_tmap_ktile_uncached(o, base, mn, k, blocks, ktiles);
   });
 }
 inline cudaError_t make_d_tmap(CUtensorMap* m, void* base, int64_t rows, int64_t cols,
