@@ -14,7 +14,11 @@ sets whose total size exceeds the 126 MB L2 (4 x 72 MB), so no step finds its in
 A second figure times single launches after a 256 MB L2-flush write ("per_launch_l2_flush").
 `e2e` is the same GEMM through the C ABI with pinned host buffers: H2D of A/SFA/B/SFB and D2H
 of D inside the timed region.  The decode shape (configs[2], M=16 N=28672 K=8192) is
-reported under "decode" in HBM GB/s, back to back over 3 rotating weight sets (396 MB).
+reported under "decode" in HBM GB/s, back to back over 3 rotating weight sets (396 MB), with
+M = 1, 64, 128 under "decode.sweep_by_M".  "prefill" is configs[3] (M=16384 N=8192 K=28672,
+1% outlier activations) and "nsplit" configs[4] (M=32768, N=65536 split over the ranks,
+K=8192; strong scaling, with the NCCL all-gather timed separately when P > 1).
+"library_baseline" times cuBLASLt's NVFP4 GEMM on the same 8192^3 operands, for comparison.
 
 --impl reference runs the reference's host GEMM (the CPU oracle's restatement of
 example/nvfp4_bf16_gemm.cu:161-168) on the host cores instead.
@@ -52,6 +56,8 @@ def parse():
                     help="main: only the 8192^3-class GEMM; decode: only the M=16 GEMM "
                          "(small runs for profiler captures; the JSON line then lacks the other)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the configs[3] prefill and configs[4] N-split legs")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--gather", action="store_true", help="also time the NCCL all-gather (P>1)")
     ap.add_argument("--no-library", action="store_true",
@@ -172,7 +178,7 @@ def barrier(world):
 # ---------------------------------------------------------------------------------------
 # workload
 # ---------------------------------------------------------------------------------------
-def make_operand(rows, K, seed, std, dev):
+def make_operand(rows, K, seed, std, dev, outlier_p=0.0, outlier_x=20.0):
     import torch
     import blackhole_b200 as bh
 
@@ -181,6 +187,10 @@ def make_operand(rows, K, seed, std, dev):
     x = torch.randn((rows, K), generator=g, device=dev, dtype=torch.float32)
     if std != 1.0:
         x.mul_(std)
+    if outlier_p > 0:  # configs[3]: a fraction of the entries multiplied (outlier channels)
+        mask = torch.rand((rows, K), generator=g, device=dev) < outlier_p
+        x[mask] *= outlier_x
+        del mask
     packed, sf, scales = bh.quantize_tensor(x)
     torch.cuda.synchronize()
     del x
@@ -377,30 +387,107 @@ def library_baseline(M, N, K, sets, steps, warmup, world):
             "steps": steps, "clocks": clk.summary()}
 
 
-def run_decode(args, dev, rank, world, hbm_peak, peak_src):
-    """The M=16 decode GEMM over 3 rotating weight sets, back to back."""
+def run_decode(args, dev, rank, world, hbm_peak, peak_src, Ms=(16, 1, 64, 128)):
+    """M x 28672 x 8192 decode GEMMs over 3 rotating weight sets (396 MB), back to
+    back.  Returns the M=16 line plus a per-M sweep."""
     import torch
 
-    Md, Nd, Kd = 16, 28672, 8192
-    dsets = []
+    Nd, Kd = 28672, 8192
+    bsets = []
     for i in range(3):
-        Ad, SFAd, scAd = make_operand(Md, Kd, 2 + 7 * i, 1.0, dev)
         Bd, SFBd, scBd = make_operand(Nd, Kd, 2000 + rank + 7 * i, 0.02, dev)
-        dsets.append((Ad, SFAd, Bd, SFBd, float(scAd[1].item() * scBd[1].item())))
-    Dd = torch.empty((Md, Nd), dtype=torch.bfloat16, device=dev)
-    dsteps = max(30, args.steps)
-    dtot = time_gemm(Md, Nd, Kd, dsets, Dd, dsteps, args.warmup, world)
-    dms = max_over_ranks(dtot / dsteps, world)
-    nbytes = gemm_bytes(Md, Nd, Kd)
-    gbs = nbytes / (dms * 1e-3) / 1e9
-    return {"workload": f"M={Md} N={Nd} K={Kd} (BASELINE configs[2]) per GPU",
-            "value": gbs * world, "unit": "GB/s", "ms_per_step": dms,
-            "bytes_per_launch": nbytes, "roofline_frac": gbs / hbm_peak,
-            "peak": hbm_peak, "peak_source": peak_src,
-            "frac_of_spec_8tbs": gbs / SPEC_HBM_GBS, "steps": dsteps,
-            "l2": "3 rotating weight sets (396 MB > 126 MB L2), back to back",
-            "host_enqueue_us_per_launch": time_gemm.host_us_per_launch,
-            "traffic": profiled_traffic(f"gemm_{Md}x{Nd}x{Kd}")}
+        bsets.append((Bd, SFBd, float(scBd[1].item())))
+    out, sweep = None, {}
+    for Md in Ms:
+        dsets = []
+        for i in range(3):
+            Ad, SFAd, scAd = make_operand(Md, Kd, 2 + 7 * i, 1.0, dev)
+            Bd, SFBd, gB = bsets[i]
+            dsets.append((Ad, SFAd, Bd, SFBd, float(scAd[1].item()) * gB))
+        Dd = torch.empty((Md, Nd), dtype=torch.bfloat16, device=dev)
+        dsteps = max(30, args.steps)
+        dtot = time_gemm(Md, Nd, Kd, dsets, Dd, dsteps, args.warmup, world)
+        dms = max_over_ranks(dtot / dsteps, world)
+        nbytes = gemm_bytes(Md, Nd, Kd)
+        gbs = nbytes / (dms * 1e-3) / 1e9
+        line = {"workload": f"M={Md} N={Nd} K={Kd} (BASELINE configs[2]) per GPU",
+                "value": gbs * world, "unit": "GB/s", "ms_per_step": dms,
+                "bytes_per_launch": nbytes, "roofline_frac": gbs / hbm_peak,
+                "peak": hbm_peak, "peak_source": peak_src,
+                "frac_of_spec_8tbs": gbs / SPEC_HBM_GBS, "steps": dsteps,
+                "l2": "3 rotating weight sets (396 MB > 126 MB L2), back to back",
+                "host_enqueue_us_per_launch": time_gemm.host_us_per_launch,
+                "traffic": profiled_traffic(f"gemm_{Md}x{Nd}x{Kd}")}
+        if Md == 16:
+            out = line
+        sweep[str(Md)] = {k: line[k] for k in ("value", "ms_per_step", "roofline_frac",
+                                                "frac_of_spec_8tbs")}
+        del dsets, Dd
+    out = dict(out or line)
+    out["sweep_by_M"] = sweep
+    return out
+
+
+def run_prefill(args, dev, rank, world, fp4_peak):
+    """M=16384 N=8192 K=28672, A from N(0,1) with 1% of entries x20, B from
+    N(0, 0.02^2); 2 rotating input sets (~800 MB), back to back."""
+    import torch
+
+    M, N, K = 16384, 8192, 28672
+    sets = []
+    for i in range(2):
+        A, SFA, sa = make_operand(M, K, 3 + 7 * i, 1.0, dev, outlier_p=0.01)
+        B, SFB, sb = make_operand(N, K, 3000 + rank + 7 * i, 0.02, dev)
+        sets.append((A, SFA, B, SFB, float(sa[1].item() * sb[1].item())))
+    D = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    steps = max(5, min(args.steps, 40))
+    tot = time_gemm(M, N, K, sets, D, steps, max(3, min(args.warmup, 5)), world)
+    ms = max_over_ranks(tot / steps, world)
+    tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+    del sets, D
+    return {"workload": f"M={M} N={N} K={K}, A with 1% outliers x20 (BASELINE configs[3]) per GPU",
+            "value": tf * world, "unit": "TFLOP/s", "ms_per_step": ms, "steps": steps,
+            "roofline_frac": tf / fp4_peak, "l2": "2 rotating input sets (~800 MB), back to back"}
+
+
+def run_nsplit(args, dev, rank, world, fp4_peak):
+    """M=32768, N=65536 split evenly over the P ranks, K=8192, seed 4; A replicated.
+    Strong scaling (the whole GEMM is fixed); with and without the NCCL all-gather of C."""
+    import torch
+    import torch.distributed as dist
+    from blackhole_b200.nsplit import shard
+
+    M, N, K = 32768, 65536, 8192
+    sh = shard(N, K, rank, world)
+    A, SFA, sa = make_operand(M, K, 4, 1.0, dev)
+    B, SFB, sb = make_operand(sh.rows, K, 4000 + rank, 1.0, dev)  # this rank's rows of B
+    alpha = float(sa[1].item() * sb[1].item())
+    D = torch.empty((M, sh.rows), dtype=torch.bfloat16, device=dev)
+    steps = max(3, min(args.steps, 10))
+    tot = time_gemm(M, sh.rows, K, [(A, SFA, B, SFB, alpha)], D, steps, 2, world)
+    ms = max_over_ranks(tot / steps, world)
+    flops = 2.0 * M * N * K
+    out = {"workload": f"M={M} N={N} K={K} split along N over {world} GPU(s) (BASELINE configs[4])",
+           "unit": "TFLOP/s", "scaling": "strong", "n_gpus": world,
+           "ms_per_step": ms, "value": flops / (ms * 1e-3) / 1e12,
+           "roofline_frac": flops / world / (ms * 1e-3) / 1e12 / fp4_peak, "steps": steps}
+    if world > 1:
+        g = torch.empty((world, M, sh.rows), dtype=torch.bfloat16, device=dev)
+        dist.all_gather_into_tensor(g, D)
+        barrier(world)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(3):
+            dist.all_gather_into_tensor(g, D)
+        e.record()
+        barrier(world)
+        gms = max_over_ranks(s.elapsed_time(e) / 3, world)
+        out["gather"] = {"ms_per_step": gms, "layout": "[P][M][N/P] bf16",
+                         "bytes_per_gpu_in": (world - 1) * M * sh.rows * 2,
+                         "with_gather_tflops": flops / ((ms + gms) * 1e-3) / 1e12}
+        del g
+    del A, SFA, B, SFB, D
+    return out
 
 
 # ---------------------------------------------------------------------------------------
@@ -427,7 +514,8 @@ def main():
             d = run_decode(args, dev, rank, world, hbm_peak, peak_src)
         assert bh.device_status(torch.cuda.current_device()) == 0
         if rank == 0:
-            print(json.dumps({"case": "decode", "decode": d, "gpu_launches": d["steps"],
+            print(json.dumps({"case": "decode", "decode": d,
+                              "gpu_launches": d["steps"] * len(d["sweep_by_M"]),
                               "clocks": clk.summary()}), flush=True)
         if world > 1:
             import torch.distributed as dist
@@ -436,6 +524,7 @@ def main():
         return
     if args.case == "main":
         args.no_decode = True
+        args.no_configs = True
 
     ROT = 4
     sets = []
@@ -485,7 +574,12 @@ def main():
 
     if not args.no_decode:
         result["decode"] = run_decode(args, dev, rank, world, hbm_peak, peak_src)
-        result["gpu_launches"] += result["decode"]["steps"]
+        result["gpu_launches"] += result["decode"]["steps"] * len(result["decode"]["sweep_by_M"])
+
+    if not args.no_configs:
+        result["prefill"] = run_prefill(args, dev, rank, world, fp4_peak)
+        result["nsplit"] = run_nsplit(args, dev, rank, world, fp4_peak)
+        result["gpu_launches"] += result["prefill"]["steps"] + result["nsplit"]["steps"]
 
     if world > 1 and args.gather:
         import torch.distributed as dist
