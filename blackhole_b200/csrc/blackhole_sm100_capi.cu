@@ -21,9 +21,9 @@
 // per CTA), so this entry point keeps that scratch in a fixed array of this module instead.
 //
 // The array holds what M <= 16 needs on a device with up to 160 SMs:
-//   flags    : 160 CTAs x 4 warps x 4 bytes + a 4-byte ticket counter, padded to 2816 bytes
+//   flags    : 160 CTAs x 8 flag words x 4 bytes + a 4-byte ticket counter, padded to 5376 bytes
 //   partials : 160 CTAs x 16 rows x 128 columns x 4 bytes = 1,310,720 bytes
-// Every GPU that loads this library holds these 1,313,536 bytes until the process exits.
+// Every GPU that loads this library holds these 1,316,096 bytes until the process exits.
 // ---------------------------------------------------------------------------------------
 namespace {
 
@@ -31,7 +31,7 @@ constexpr int kNoAllocMaxM = 16;
 constexpr int kNoAllocMaxSms = 160;
 constexpr size_t kNoAllocScratchBytes = static_cast<size_t>(
     blackhole::sm100::nvfp4_skinny_workspace_bytes(kNoAllocMaxSms, kNoAllocMaxM));
-static_assert(kNoAllocScratchBytes == 1313536, "documented size of the scratch array");
+static_assert(kNoAllocScratchBytes == 1316096, "documented size of the scratch array");
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 

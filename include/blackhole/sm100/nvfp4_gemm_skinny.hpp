@@ -20,7 +20,7 @@
 //     (deterministic) and writes BF16.  Only warps exchange data, never whole CTAs, so no
 //     CTA-wide barrier sits in the epilogue.
 //
-// Each CTA parks at most one partial, so the workspace is 4 flags per CTA plus
+// Each CTA parks at most one partial, so the workspace is 8 flags per CTA plus
 // grid * MPAD * 128 * 4 bytes of partials (nvfp4_skinny_workspace_bytes).
 // Flags are raised to 1 by the producer of a partial and reset to 0 by its consumer, so a
 // workspace is reusable by later launches on the same stream (and by graph replays).
@@ -52,7 +52,12 @@ struct Nvfp4SkinnyTraits {
   // work, s = RangeSkew / 64
   static constexpr int RangeSkew = 6;
 
-  static constexpr int NumWarps = 6;                        // TMA, MMA, 4 x epilogue
+  // TMA, MMA, then 4 epilogue warps (one per TMEM sub-partition), or 8 for MPAD >= 64: two per
+  // sub-partition, each draining half of the accumulator columns (the last segment's
+  // epilogue is on the kernel's critical path; at MPAD = 128 it took ~11 us with 4 warps).
+  static constexpr int NumEpiWarps = MPAD >= 64 ? 8 : 4;
+  static constexpr int EpiCols = MPAD * 4 / NumEpiWarps;    // accumulator columns per warp
+  static constexpr int NumWarps = 2 + NumEpiWarps;
   static constexpr int NumThreads = NumWarps * 32;
   static constexpr int ProducerWarp = 0;
   static constexpr int MmaWarp = 1;
@@ -69,12 +74,13 @@ struct Nvfp4SkinnyTraits {
   static_assert(MPAD % 16 == 0 && MPAD >= 16 && MPAD <= 128, "UMMA N");
 };
 
-// Workspace layout: flag words first, at a fixed place for the device (4 per possible CTA,
-// then the ticket counter, padded to 256 bytes), then the FP32 partials.  Keeping the flags at
-// a fixed offset means a workspace shared by calls of different M never sees partial data
-// where a flag should be.
+// Workspace layout: flag words first, at a fixed place for the device (8 per possible CTA:
+// one per epilogue warp, then the ticket counter, padded to 256 bytes), then the FP32
+// partials.  Keeping the flags at a fixed offset means a workspace shared by calls of
+// different M never sees partial data where a flag should be.
+constexpr int kSkinnyFlagsPerCta = 8;
 constexpr int64_t nvfp4_skinny_flag_bytes(int num_sms) {
-  return (int64_t(num_sms) * 16 + 16 + 255) / 256 * 256;
+  return (int64_t(num_sms) * 4 * kSkinnyFlagsPerCta + 16 + 255) / 256 * 256;
 }
 // Bytes of workspace the skinny schedule needs on a device with num_sms SMs at width mpad.
 constexpr int64_t nvfp4_skinny_workspace_bytes(int num_sms, int mpad) {
@@ -92,7 +98,7 @@ struct Nvfp4SkinnyParams {
   const uint8_t* sfx;   // SFA
   uint16_t* d;
   float* ws;            // [grid][MPAD][128] partials
-  uint32_t* flags;      // [grid][4]: one per epilogue warp
+  uint32_t* flags;      // [grid][8]: one per epilogue warp
   uint32_t* ticket;     // entry counter: CTAs take ranges in the order they start
   uint32_t* status;
   float alpha;
@@ -216,7 +222,7 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(acc_full(a), 1);
-      mbar_init(acc_empty(a), 4);
+      mbar_init(acc_empty(a), KT::NumEpiWarps);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -368,14 +374,17 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------ epilogue ----------------------------------------
-    const int q = warp & 3;
+    constexpr int EC = KT::EpiCols;
+    const int q = warp & 3;                                       // TMEM sub-partition
+    const int m0 = ((warp - KT::FirstEpiWarp) >> 2) * EC;        // first column (row of D)
+    const int fi = q + 4 * ((warp - KT::FirstEpiWarp) >> 2);     // this warp's flag slot
     const int n_local = 32 * q + lane;                            // row of the B block
     // Adds the FP32 partials parked by the earlier CTAs sharing row block sg.rb (in a fixed
     // order: deterministic) into v; false if a bounded wait gave up.
-    auto add_partials = [&](const Segment& sg, float (&v)[MPAD]) -> bool {
+    auto add_partials = [&](const Segment& sg, float (&v)[EC]) -> bool {
       const int64_t rb0 = int64_t(sg.rb) * p.kt_per_rb;
       for (int cc = c - 1; cc >= 0 && range_start(p, cc + 1) > rb0; --cc) {
-        uint32_t* flag = p.flags + 4 * cc + q;
+        uint32_t* flag = p.flags + kSkinnyFlagsPerCta * cc + fi;
         int ready = 1;
         if (lane == 0) {
           const uint64_t t0 = globaltimer_ns();
@@ -392,38 +401,39 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
         ready = __shfl_sync(0xFFFFFFFFu, ready, 0);
         if (!ready) return false;
         (void)ld_acquire(flag);
-        const float* src = p.ws + (int64_t(cc) * MPAD) * 128 + n_local;
+        const float* src = p.ws + (int64_t(cc) * MPAD + m0) * 128 + n_local;
 #pragma unroll
-        for (int m = 0; m < MPAD; ++m)
-          if (m < p.M) v[m] += __ldcg(src + m * 128);
+        for (int m = 0; m < EC; ++m)
+          if (m0 + m < p.M) v[m] += __ldcg(src + m * 128);
         __syncwarp();
         if (lane == 0) st_release(flag, 0u);
       }
       return true;
     };
-    // For narrow MPAD the partials of a finished row block are fetched before its
-    // accumulator is ready, so that their latency is off the critical path.
-    constexpr bool kEarlyPartials = MPAD <= 32;
+    // When a warp drains at most 32 columns, the partials of a finished row block are
+    // fetched before its accumulator is ready, so that their latency is off the critical path.
+    constexpr bool kEarlyPartials = EC <= 32;
     int acc = 0;
     uint32_t acc_phase = 0;
     SegmentWalk w = walk(p, c);
     Segment sg;
     while (w.next(sg)) {
       const bool finisher = sg.kt1 == p.kt_per_rb;
-      float part[kEarlyPartials ? MPAD : 1];
+      float part[kEarlyPartials ? EC : 1];
       if constexpr (kEarlyPartials) {
 #pragma unroll
-        for (int m = 0; m < MPAD; ++m) part[m] = 0.f;
+        for (int m = 0; m < EC; ++m) part[m] = 0.f;
         if (finisher && sg.kt0 > 0 && !add_partials(sg, part)) break;
       }
       if (!wait_bounded_warp(acc_full(acc), acc_phase, abort_flag, p.status, kStatusEpilogueTimeout))
         break;
       tc_fence_after();
-      float v[MPAD];
+      float v[EC];
       {
-        const uint32_t t = tmem + (static_cast<uint32_t>(32 * q) << 16) + KT::AccStride * acc;
+        const uint32_t t =
+            tmem + (static_cast<uint32_t>(32 * q) << 16) + KT::AccStride * acc + uint32_t(m0);
 #pragma unroll
-        for (int j = 0; j < MPAD / 16; ++j) {
+        for (int j = 0; j < EC / 16; ++j) {
           uint32_t r[16];
           tmem_ld_32x32b_x16(t + 16 * j, r);
           tmem_ld_wait();
@@ -445,27 +455,27 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
       const int n = sg.rb * 128 + n_local;
       if (!finisher) {
         // Partial of a row block finished by a later CTA: park it, then raise this warp's flag.
-        float* dst = p.ws + (int64_t(c) * MPAD) * 128 + n_local;
+        float* dst = p.ws + (int64_t(c) * MPAD + m0) * 128 + n_local;
 #pragma unroll
-        for (int m = 0; m < MPAD; ++m)
-          if (m < p.M) __stcg(dst + m * 128, v[m]);
+        for (int m = 0; m < EC; ++m)
+          if (m0 + m < p.M) __stcg(dst + m * 128, v[m]);
         __threadfence();
         __syncwarp();
-        if (lane == 0) st_release(p.flags + 4 * c + q, 1u);
+        if (lane == 0) st_release(p.flags + kSkinnyFlagsPerCta * c + fi, 1u);
         continue;
       }
       if constexpr (kEarlyPartials) {
 #pragma unroll
-        for (int m = 0; m < MPAD; ++m) v[m] += part[m];
+        for (int m = 0; m < EC; ++m) v[m] += part[m];
       } else {
         if (sg.kt0 > 0 && !add_partials(sg, v)) break;
       }
       const float a = p.alpha;
 #pragma unroll
-      for (int m = 0; m < MPAD; ++m) {
-        if (m < p.M) {
+      for (int m = 0; m < EC; ++m) {
+        if (m0 + m < p.M) {
           __nv_bfloat16 b = __float2bfloat16_rn(a * v[m]);
-          p.d[int64_t(m) * p.N + n] = *reinterpret_cast<uint16_t*>(&b);
+          p.d[int64_t(m0 + m) * p.N + n] = *reinterpret_cast<uint16_t*>(&b);
         }
       }
     }
@@ -507,7 +517,7 @@ inline cudaError_t launch_skinny(int M, int N, int K, const void* A, const void*
   p.sfx = static_cast<const uint8_t*>(SFA);
   p.d = static_cast<uint16_t*>(D);
   p.flags = static_cast<uint32_t*>(ws);
-  p.ticket = p.flags + 4 * st->num_sms;
+  p.ticket = p.flags + kSkinnyFlagsPerCta * st->num_sms;
   p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + nvfp4_skinny_flag_bytes(st->num_sms));
   p.status = st->status;
   p.alpha = alpha;

@@ -93,7 +93,7 @@ BLACKHOLE_SM100_API int blackhole_sm100_nvfp4_quantize(const void* X, int x_is_b
  * For callers that may not allocate device memory when they run the GEMM (memory planned
  * up front, no cudaMalloc synchronisation allowed on the path, or a host that passes only
  * the input and output buffers).  It runs the skinny schedule with its scratch held in a
- * fixed 1,313,536-byte array inside this library, sized for M <= 16 on devices with at most
+ * fixed 1,316,096-byte array inside this library, sized for M <= 16 on devices with at most
  * 160 SMs; larger M or more SMs return cudaErrorInvalidValue.  It calls no cudaMalloc or
  * cudaFree.  The first call on each device looks up the array's device address with
  * cudaGetSymbolAddress; make that first call before any stream capture.  Every call uses the

@@ -101,3 +101,61 @@ def test_config1_8192_cubed_sampled():
     assert bad == 0, f"{bad} bad (max err {maxerr}, err/tol {ratio})"
     assert rel <= 0.05
     assert not np.any(got == 0xFFFF), "unwritten output elements"
+
+
+def _device_operands(M, N, K, seed_a, seed_b, std_b, outlier_p=0.0):
+    """Operands built on the device the way bench.py builds them (torch generator + this
+    library's quantiser, which is bit-exact with the oracle's), copied back for the oracle."""
+    import torch
+    import blackhole_b200 as bh
+
+    dev = torch.device("cuda:0")
+    ga = torch.Generator(device=dev)
+    ga.manual_seed(seed_a)
+    xa = torch.randn((M, K), generator=ga, device=dev)
+    if outlier_p > 0:
+        mask = torch.rand((M, K), generator=ga, device=dev) < outlier_p
+        xa[mask] *= 20.0
+        del mask
+    gb = torch.Generator(device=dev)
+    gb.manual_seed(seed_b)
+    xb = torch.randn((N, K), generator=gb, device=dev) * std_b
+    A, SFA, sa = bh.quantize_tensor(xa)
+    B, SFB, sb = bh.quantize_tensor(xb)
+    del xa, xb
+    alpha = float(sa[1].item() * sb[1].item())
+    return (A, SFA, B, SFB, alpha), tuple(t.cpu().numpy().reshape(-1) for t in (A, SFA, B, SFB))
+
+
+def test_config3_prefill_outliers_full_size_sampled():
+    """M=16384 N=8192 K=28672, 1% of the activations x20, weights N(0, 0.02^2)."""
+    import torch
+    import blackhole_b200 as bh
+
+    M, N, K = 16384, 8192, 28672
+    (A, SFA, B, SFB, alpha), host = _device_operands(M, N, K, 3, 3000, 0.02, outlier_p=0.01)
+    D = torch.full((M, N), -1, dtype=torch.int16, device="cuda:0")
+    bh.nvfp4_bf16_gemm(M, N, K, A, SFA, B, SFB, D, alpha)
+    torch.cuda.synchronize()
+    assert bh.device_status(0) == 0
+    got = D.cpu().numpy().view(np.uint16)
+    bad, maxerr, ratio, rel = C.check_sampled(M, N, K, *host, alpha, got, S=4096, seed=33)
+    assert bad == 0, f"{bad} bad (max err {maxerr}, err/tol {ratio})"
+    assert not np.any(got == 0xFFFF), "unwritten output elements"
+
+
+def test_config4_shard_full_size_sampled():
+    """configs[4] at P = 8: the per-GPU GEMM of one rank (M=32768, N=65536/8, K=8192)."""
+    import torch
+    import blackhole_b200 as bh
+
+    M, N, K = 32768, 8192, 8192
+    (A, SFA, B, SFB, alpha), host = _device_operands(M, N, K, 4, 4003, 1.0)
+    D = torch.full((M, N), -1, dtype=torch.int16, device="cuda:0")
+    bh.nvfp4_bf16_gemm(M, N, K, A, SFA, B, SFB, D, alpha)
+    torch.cuda.synchronize()
+    assert bh.device_status(0) == 0
+    got = D.cpu().numpy().view(np.uint16)
+    bad, maxerr, ratio, rel = C.check_sampled(M, N, K, *host, alpha, got, S=4096, seed=44)
+    assert bad == 0, f"{bad} bad (max err {maxerr}, err/tol {ratio})"
+    assert not np.any(got == 0xFFFF), "unwritten output elements"
