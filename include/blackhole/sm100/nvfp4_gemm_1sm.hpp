@@ -89,7 +89,7 @@ struct Nvfp4GemmParams {
   int tiles_m, tiles_n, num_tiles;
   int k_tiles;
   int sf_k_atoms;       // 512-byte SF atoms along K per 128-row block
-  int n_blocks128;      // N / 128
+  int n_blocks128;      // 128-row blocks of B (and of SFB): ceil(N / 128)
 };
 
 
@@ -346,7 +346,7 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
           }
           fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0 && live) {
+          if (lane == 0 && live && col0 + c32 + 16 * h < p.N) {
             tma_store_2d(&p.tmap_d, box, col0 + c32 + 16 * h, row0, pol_d);
             bulk_commit_group();
           }
@@ -397,7 +397,7 @@ inline cudaError_t launch_1sm(int M, int N, int K, const void* A, const void* SF
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.k_tiles = K / KT::TileK;
   p.sf_k_atoms = static_cast<int>(sf_k_atoms(K));
-  p.n_blocks128 = N / 128;
+  p.n_blocks128 = (N + 127) / 128;
   const int grid = p.num_tiles < st->num_sms ? p.num_tiles : st->num_sms;
   e = launch_pdl(nvfp4_gemm_kernel<KT>, dim3(grid), dim3(KT::NumThreads), KT::SmemBytes, stream, p);
   if (e != cudaSuccess) return e;

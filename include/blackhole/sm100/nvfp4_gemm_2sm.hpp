@@ -82,7 +82,7 @@ struct Nvfp4Gemm2SmParams {
   CUtensorMap tmap_a;     // A  [M][K/2] bytes, box 128 x 128 B, 128B swizzle
   CUtensorMap tmap_b;     // B  [N][K/2] bytes, box 128 x 128 B, 128B swizzle
   CUtensorMap tmap_sfa;   // SFA [M/128][K/256][2048 B], box one block x one k-tile
-  CUtensorMap tmap_sfb;   // SFB [N/128][K/256][2048 B], box two blocks x one k-tile
+  CUtensorMap tmap_sfb;   // SFB [ceil(N/128)][K/256][2048 B], box two blocks x one k-tile
   CUtensorMap tmap_d;     // D  [M][N] bf16, box 32 rows x 64 columns, 128B swizzle
   uint32_t* status;
   float alpha;

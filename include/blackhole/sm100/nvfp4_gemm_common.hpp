@@ -34,11 +34,12 @@ enum : uint32_t {
 
 // Shape / alignment check shared by every schedule and the C ABI (host only, no CUDA calls).
 // The reference accepts M % 128 == 0, N % 128 == 0, K % 256 == 0 (nvfp4_gemm.hpp:594-596);
-// here any M >= 1 is accepted.
+// here any M >= 1 and any N % 8 == 0 are accepted (tiles past M / N read zeros through TMA and
+// are clipped on store; N % 8 keeps D's rows 16-byte aligned for the TMA stores).
 inline cudaError_t nvfp4_check_args(int M, int N, int K, const void* A, const void* SFA,
                                     const void* B, const void* SFB, const void* D) {
-  if (M < 1 || N < 128 || K < 256) return cudaErrorInvalidValue;
-  if (N % 128 != 0 || K % 256 != 0) return cudaErrorInvalidValue;
+  if (M < 1 || N < 8 || K < 256) return cudaErrorInvalidValue;
+  if (N % 8 != 0 || K % 256 != 0) return cudaErrorInvalidValue;
   if (!A || !SFA || !B || !SFB || !D) return cudaErrorInvalidValue;
   auto mis = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) != 0; };
   if (mis(A) || mis(SFA) || mis(B) || mis(SFB) || mis(D)) return cudaErrorInvalidValue;

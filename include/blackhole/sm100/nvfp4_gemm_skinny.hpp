@@ -8,7 +8,7 @@
 // and the M activation rows become the UMMA N (padded to MPAD = 16/32/64/128; TMA
 // zero-fills rows >= M):
 //
-//   * work unit = (128-row block rb of B, 256-wide k-tile kt); U = N/128 * K/256 units are
+//   * work unit = (128-row block rb of B, 256-wide k-tile kt); U = ceil(N/128) * K/256 units are
 //     split into equal contiguous ranges, one per persistent CTA (stream-K), so every SM
 //     streams the same number of bytes;
 //   * each CTA walks its range backwards in row-block segments; a segment accumulates in
@@ -104,7 +104,7 @@ struct Nvfp4SkinnyParams {
   float alpha;
   int M, N, K;
   int kt_per_rb;        // K / 256
-  int64_t units;        // N/128 * K/256
+  int64_t units;        // ceil(N/128) * K/256
   int grid;
   int skew;             // range of ticket t shrinks linearly: density (1 + s - 2 s t / grid), s = skew/64
   int sf_k_atoms;
@@ -479,7 +479,7 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
       const float a = p.alpha;
 #pragma unroll
       for (int m = 0; m < EC; ++m) {
-        if (m0 + m < p.M) {
+        if (m0 + m < p.M && n < p.N) {
           __nv_bfloat16 b = __float2bfloat16_rn(a * v[m]);
           p.d[int64_t(m0 + m) * p.N + n] = *reinterpret_cast<uint16_t*>(&b);
         }
@@ -515,7 +515,7 @@ inline cudaError_t launch_skinny(int M, int N, int K, const void* A, const void*
   e = make_kmajor_tmap(&p.tmap_x, A, M, K / 2, KT::MPAD);
   if (e != cudaSuccess) return e;
   p.kt_per_rb = K / KT::TileK;
-  p.units = int64_t(N / 128) * p.kt_per_rb;
+  p.units = int64_t((N + 127) / 128) * p.kt_per_rb;
   int grid = grid_cap < st->num_sms ? grid_cap : st->num_sms;
   if (p.units < grid) grid = static_cast<int>(p.units);
   if (nvfp4_skinny_workspace_bytes(st->num_sms, KT::MPAD) > ws_bytes) return cudaErrorInvalidValue;

@@ -69,3 +69,13 @@ def test_skinny_rejects_large_m_and_short_workspace():
         bh.nvfp4_bf16_gemm_ex(16, 128, 256, A, SF, A, SF, D, schedule="skinny", workspace=small)
     torch.cuda.synchronize()
     assert bh.device_status(0) == 0
+
+
+@pytest.mark.parametrize("schedule,M,N,K", [
+    ("1sm", 256, 200, 512), ("1sm", 300, 1000, 768), ("2sm", 512, 136, 512),
+    ("2sm", 640, 1304, 1024), ("skinny", 16, 1000, 2048), ("skinny", 7, 8, 256),
+    ("skinny", 100, 2056, 1024), ("auto", 1024, 3000, 512)])
+def test_ragged_n(schedule, M, N, K):
+    """N not a multiple of 128 (only N % 8 == 0): B rows and SFB blocks past N read zeros, D
+    columns past N are never written."""
+    _check(M, N, K, schedule, seed=M + 7 * N + K)
