@@ -107,7 +107,7 @@ def nvfp4_bf16_gemm(M: int, N: int, K: int, A, SFA, B, SFB, D, alpha: float = 1.
     A (M x K/2 bytes, E2M1 packed, low nibble = even k), SFA (UE4M3, 128x4 layout,
     sf_storage_bytes(M, K) bytes), B (N x K/2), SFB, D (M x N bf16, row-major).
     Raises BlackholeError(cudaErrorInvalidValue) for unsupported shapes
-    (M >= 1, N % 8 == 0, K % 256 == 0), null or misaligned pointers.
+    (M >= 1, N % 8 == 0, K % 32 == 0), null or misaligned pointers.
     """
     rc = load().blackhole_sm100_nvfp4_bf16_gemm(
         int(M), int(N), int(K), _ptr(A), _ptr(SFA), _ptr(B), _ptr(SFB), _ptr(D),

@@ -26,8 +26,9 @@
 //                tile, which on B200 is what limits the tensor pipe once the kernel is power
 //                capped (measured at 8192^3 with N(0,1) data: 220.8 us vs 226.5 us per launch).
 //
-// Shapes: M >= 1, N % 8 == 0, K % 256 == 0.  The reference additionally requires
-// M % 128 == 0 and N % 128 == 0 (nvfp4_gemm.hpp:594).  Every mbarrier wait in the kernels is
+// Shapes: M >= 1, N % 8 == 0, K % 32 == 0.  The reference requires M % 128 == 0,
+// N % 128 == 0 and K % 256 == 0 (nvfp4_gemm.hpp:594).  With a K tail, the scale factors of
+// the K-groups past K (padding of the last 128x4 atom) must be finite: they multiply zeros.  Every mbarrier wait in the kernels is
 // bounded: a stalled pipeline records a status bit (blackhole_sm100_device_status) and returns.
 // =====================================================================================
 

@@ -90,6 +90,9 @@ struct Nvfp4GemmParams {
   int k_tiles;
   int sf_k_atoms;       // 512-byte SF atoms along K per 128-row block
   int n_blocks128;      // 128-row blocks of B (and of SFB): ceil(N / 128)
+  int sf_tail;          // K % TileK != 0: scale factors through the atom-granular tensor maps
+  CUtensorMap tmap_sfa; // (sf_tail only) SFA [M/128][atoms][512 B], box 4 atoms x 1 block
+  CUtensorMap tmap_sfb; // (sf_tail only) SFB [N/128][atoms][512 B], box 4 atoms x 2 blocks
 };
 
 
@@ -159,6 +162,10 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
     prefetch_tmap(&p.tmap_a);
     prefetch_tmap(&p.tmap_b);
     prefetch_tmap(&p.tmap_d);
+    if (p.sf_tail) {
+      prefetch_tmap(&p.tmap_sfa);
+      prefetch_tmap(&p.tmap_sfb);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -181,7 +188,8 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
         detail::tile_coords<KT>(tile, p, m_blk, n_blk);
         const bool sfb_hi = (2 * n_blk + 1) < p.n_blocks128;
         const uint32_t bytes =
-            KT::ABytes + KT::BBytes + KT::SFABytes + (sfb_hi ? KT::SFBBytes : KT::SFBBytes / 2);
+            KT::ABytes + KT::BBytes + KT::SFABytes +
+            ((sfb_hi || p.sf_tail) ? KT::SFBBytes : KT::SFBBytes / 2);
         const uint8_t* sfa_src = p.sfa + (int64_t(m_blk) * p.sf_k_atoms) * 512;
         const uint8_t* sfb_src0 = p.sfb + (int64_t(2 * n_blk) * p.sf_k_atoms) * 512;
         const uint8_t* sfb_src1 = sfb_src0 + int64_t(p.sf_k_atoms) * 512;
@@ -198,11 +206,18 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
           tma_load_2d(sB + stage * KT::BBytes, &p.tmap_b, fb, kt * KT::RowBytes, n_blk * KT::TileN,
                       pol_b);
           const int64_t k_off = int64_t(kt) * KT::KSteps * 512;
-          bulk_load(sSFA + stage * KT::SFABytes, sfa_src + k_off, KT::SFABytes, fb, pol_a);
-          bulk_load(sSFB + stage * KT::SFBBytes, sfb_src0 + k_off, KT::SFBBytes / 2, fb, pol_b);
-          if (sfb_hi)
-            bulk_load(sSFB + stage * KT::SFBBytes + KT::SFBBytes / 2, sfb_src1 + k_off,
-                      KT::SFBBytes / 2, fb, pol_b);
+          if (p.sf_tail) {  // atoms past K (and blocks past N) read zeros
+            tma_load_3d(sSFA + stage * KT::SFABytes, &p.tmap_sfa, fb, 0, KT::KSteps * kt, m_blk,
+                        pol_a);
+            tma_load_3d(sSFB + stage * KT::SFBBytes, &p.tmap_sfb, fb, 0, KT::KSteps * kt,
+                        2 * n_blk, pol_b);
+          } else {
+            bulk_load(sSFA + stage * KT::SFABytes, sfa_src + k_off, KT::SFABytes, fb, pol_a);
+            bulk_load(sSFB + stage * KT::SFBBytes, sfb_src0 + k_off, KT::SFBBytes / 2, fb, pol_b);
+            if (sfb_hi)
+              bulk_load(sSFB + stage * KT::SFBBytes + KT::SFBBytes / 2, sfb_src1 + k_off,
+                        KT::SFBBytes / 2, fb, pol_b);
+          }
           ++issued;
           if (++stage == S) {
             stage = 0;
@@ -395,9 +410,17 @@ inline cudaError_t launch_1sm(int M, int N, int K, const void* A, const void* SF
   p.tiles_m = (M + KT::TileM - 1) / KT::TileM;
   p.tiles_n = (N + KT::TileN - 1) / KT::TileN;
   p.num_tiles = p.tiles_m * p.tiles_n;
-  p.k_tiles = K / KT::TileK;
+  p.k_tiles = (K + KT::TileK - 1) / KT::TileK;
   p.sf_k_atoms = static_cast<int>(sf_k_atoms(K));
   p.n_blocks128 = (N + 127) / 128;
+  p.sf_tail = K % KT::TileK != 0;
+  if (p.sf_tail) {
+    if (KT::KSteps != 4) return cudaErrorInvalidValue;  // the tail maps fetch 4 atoms per k-tile
+    e = make_sf_tmap_atoms(&p.tmap_sfa, SFA, M, K, 1);
+    if (e != cudaSuccess) return e;
+    e = make_sf_tmap_atoms(&p.tmap_sfb, SFB, N, K, 2);
+    if (e != cudaSuccess) return e;
+  }
   const int grid = p.num_tiles < st->num_sms ? p.num_tiles : st->num_sms;
   e = launch_pdl(nvfp4_gemm_kernel<KT>, dim3(grid), dim3(KT::NumThreads), KT::SmemBytes, stream, p);
   if (e != cudaSuccess) return e;

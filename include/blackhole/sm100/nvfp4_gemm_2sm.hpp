@@ -90,6 +90,7 @@ struct Nvfp4Gemm2SmParams {
   int tiles_m, tiles_n, num_tiles;
   int k_tiles;
   int sf_k_atoms;
+  int sf_tail;            // K % 256 != 0: tmap_sfa / tmap_sfb are atom-granular (y = atom)
 };
 
 namespace detail {
@@ -197,8 +198,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
           tma_load_2d_pair(sA + stage * KT::ABytes, &p.tmap_a, lb, kt * KT::RowBytes, a_row, pol);
           tma_load_2d_pair(sB + stage * KT::BBytes, &p.tmap_b, lb, kt * KT::RowBytes, b_row, pol);
           // one request per operand: SFA as one 2 KB row, SFB as the pair's two 2 KB rows
-          tma_load_3d_pair(sSFA + stage * KT::SFABytes, &p.tmap_sfa, lb, 0, kt, sfa_blk, pol);
-          tma_load_3d_pair(sSFB + stage * KT::SFBBytes, &p.tmap_sfb, lb, 0, kt, sfb_blk, pol);
+          const int sf_y = p.sf_tail ? KT::KSteps * kt : kt;
+          tma_load_3d_pair(sSFA + stage * KT::SFABytes, &p.tmap_sfa, lb, 0, sf_y, sfa_blk, pol);
+          tma_load_3d_pair(sSFB + stage * KT::SFBBytes, &p.tmap_sfb, lb, 0, sf_y, sfb_blk, pol);
           ++issued;
           if (++stage == S) {
             stage = 0;
@@ -378,9 +380,13 @@ inline cudaError_t launch_2sm(int M, int N, int K, const void* A, const void* SF
   if (e != cudaSuccess) return e;
   e = make_kmajor_tmap(&p.tmap_b, B, N, K / 2, KT::CtaN, KT::RowBytes);
   if (e != cudaSuccess) return e;
-  e = make_sf_tmap_ktile(&p.tmap_sfa, SFA, M, K, 1, 1);
+  // K % 256 != 0: 4 rows of 512 B per block, so that the K tail reads zeros (slower per k-tile)
+  p.sf_tail = K % KT::TileK != 0;
+  e = p.sf_tail ? make_sf_tmap_atoms(&p.tmap_sfa, SFA, M, K, 1)
+                : make_sf_tmap_ktile(&p.tmap_sfa, SFA, M, K, 1, 1);
   if (e != cudaSuccess) return e;
-  e = make_sf_tmap_ktile(&p.tmap_sfb, SFB, N, K, 2, 1);
+  e = p.sf_tail ? make_sf_tmap_atoms(&p.tmap_sfb, SFB, N, K, 2)
+                : make_sf_tmap_ktile(&p.tmap_sfb, SFB, N, K, 2, 1);
   if (e != cudaSuccess) return e;
   e = make_d_tmap(&p.tmap_d, D, M, N);
   if (e != cudaSuccess) return e;
@@ -392,7 +398,7 @@ inline cudaError_t launch_2sm(int M, int N, int K, const void* A, const void* SF
   p.tiles_m = (M + KT::TileM - 1) / KT::TileM;
   p.tiles_n = (N + KT::TileN - 1) / KT::TileN;
   p.num_tiles = p.tiles_m * p.tiles_n;
-  p.k_tiles = K / KT::TileK;
+  p.k_tiles = (K + KT::TileK - 1) / KT::TileK;
   p.sf_k_atoms = static_cast<int>(sf_k_atoms(K));
   // Persistent grid = the number of 2-CTA clusters that can be resident at once.  GPCs with
   // an odd number of usable SMs leave an SM idle, so this is below num_sms / 2; launching

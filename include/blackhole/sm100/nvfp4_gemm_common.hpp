@@ -34,12 +34,13 @@ enum : uint32_t {
 
 // Shape / alignment check shared by every schedule and the C ABI (host only, no CUDA calls).
 // The reference accepts M % 128 == 0, N % 128 == 0, K % 256 == 0 (nvfp4_gemm.hpp:594-596);
-// here any M >= 1 and any N % 8 == 0 are accepted (tiles past M / N read zeros through TMA and
-// are clipped on store; N % 8 keeps D's rows 16-byte aligned for the TMA stores).
+// here any M >= 1, N % 8 == 0 and K % 32 == 0 are accepted (tiles past M / N / K read zeros
+// through TMA and are clipped on store; N % 8 keeps D's rows and K % 32 the packed rows of A
+// and B 16-byte aligned for TMA).
 inline cudaError_t nvfp4_check_args(int M, int N, int K, const void* A, const void* SFA,
                                     const void* B, const void* SFB, const void* D) {
-  if (M < 1 || N < 8 || K < 256) return cudaErrorInvalidValue;
-  if (N % 8 != 0 || K % 256 != 0) return cudaErrorInvalidValue;
+  if (M < 1 || N < 8 || K < 32) return cudaErrorInvalidValue;
+  if (N % 8 != 0 || K % 32 != 0) return cudaErrorInvalidValue;
   if (!A || !SFA || !B || !SFB || !D) return cudaErrorInvalidValue;
   auto mis = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) != 0; };
   if (mis(A) || mis(SFA) || mis(B) || mis(SFB) || mis(D)) return cudaErrorInvalidValue;
@@ -185,6 +186,26 @@ inline cudaError_t make_sf_tmap_ktile_uncached(CUtensorMap* m, const void* base,
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+// Scale factors as a 3-D tensor [row blocks][atoms][512 B] for K % 256 != 0: a box of
+// {512 B, 4 atoms, blocks} lands as [block][atom][512 B], the same layout as the k-tile map,
+// and atoms past the last one of a block (the K tail) read zeros instead of running into the
+// next block or past the end of the buffer.
+inline cudaError_t make_sf_tmap_atoms_uncached(CUtensorMap* m, const void* base, int64_t mn,
+                                               int64_t k, uint32_t blocks) {
+  EncodeTiledFn enc = encode_tiled_fn();
+  if (!enc) return cudaErrorNotSupported;
+  const int64_t k_atoms = sf_k_atoms(k);
+  cuuint64_t dims[3] = {64u, static_cast<cuuint64_t>(k_atoms),
+                        static_cast<cuuint64_t>((mn + 127) / 128)};
+  cuuint64_t strides[2] = {512u, static_cast<cuuint64_t>(k_atoms * 512)};
+  cuuint32_t box[3] = {64u, 4u, blocks};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<void*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 // Row-major BF16 [rows][cols] output with a (32 rows x box_cols columns) box: the store box
 // of one epilogue warp.  Parts of a box past the tensor edge are not written.
 // box_cols = 64 (128-byte rows, 128B swizzle) or 16 (32-byte rows, 32B swizzle).
@@ -221,6 +242,12 @@ inline cudaError_t make_sf_tmap_ktile(CUtensorMap* m, const void* base, int64_t 
                                       uint32_t blocks, uint32_t ktiles) {
   return cached_tmap({3, base, mn, k, blocks, ktiles}, m, [&](CUtensorMap* o) {
     return make_sf_tmap_ktile_uncached(o, base, mn, k, blocks, ktiles);
+  });
+}
+inline cudaError_t make_sf_tmap_atoms(CUtensorMap* m, const void* base, int64_t mn, int64_t k,
+                                      uint32_t blocks) {
+  return cached_tmap({4, base, mn, k, blocks, 0}, m, [&](CUtensorMap* o) {
+    return make_sf_tmap_atoms_uncached(o, base, mn, k, blocks);
   });
 }
 inline cudaError_t make_d_tmap(CUtensorMap* m, void* base, int64_t rows, int64_t cols,

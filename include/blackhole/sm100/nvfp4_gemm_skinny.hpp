@@ -103,12 +103,15 @@ struct Nvfp4SkinnyParams {
   uint32_t* status;
   float alpha;
   int M, N, K;
-  int kt_per_rb;        // K / 256
-  int64_t units;        // ceil(N/128) * K/256
+  int kt_per_rb;        // ceil(K / 256)
+  int64_t units;        // ceil(N/128) * ceil(K/256)
   int grid;
   int skew;             // range of ticket t shrinks linearly: density (1 + s - 2 s t / grid), s = skew/64
   int sf_k_atoms;
   int l2_pf;            // k-tiles of B / SFB prefetched into L2 before the previous kernel completes
+  int sf_tail;          // K % 256 != 0: scale factors through the atom-granular tensor maps
+  CUtensorMap tmap_sfw; // (sf_tail only) SFB [N/128][atoms][512 B], box 4 atoms x 1 block
+  CUtensorMap tmap_sfx; // (sf_tail only) SFA [1][atoms][512 B], box 4 atoms
 };
 
 namespace skinny_detail {
@@ -270,8 +273,10 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
         }
         const int kt = kta++;
         tma_prefetch_l2_2d(&p.tmap_w, kt * KT::RowBytes, sa.rb * KT::TileW);
+        // only the atoms that exist (the last k-tile of a K tail has fewer than 4)
+        const int atoms = min(KT::KSteps, p.sf_k_atoms - KT::KSteps * kt);
         bulk_prefetch_l2(p.sfw + int64_t(sa.rb) * p.sf_k_atoms * 512 + int64_t(kt) * KT::KSteps * 512,
-                         KT::SFBytes);
+                         uint32_t(atoms) * 512u);
       };
       for (int i = 0; i < p.l2_pf; ++i) prefetch_next();
       pdl_wait_prior_grid();
@@ -293,9 +298,15 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
           mbar_arrive_expect_tx(fb, KT::StageBytes);
           // A (small, L2-resident) ahead of B in the copy engine's queue
           tma_load_2d(st_x(stage), &p.tmap_x, fb, kt * KT::RowBytes, 0, pol_x);
-          bulk_load(st_sfx(stage), p.sfx + k_off, KT::SFBytes, fb, pol_x);
+          if (p.sf_tail)  // atoms past K read zeros
+            tma_load_3d(st_sfx(stage), &p.tmap_sfx, fb, 0, KT::KSteps * kt, 0, pol_x);
+          else
+            bulk_load(st_sfx(stage), p.sfx + k_off, KT::SFBytes, fb, pol_x);
           tma_load_2d(st_w(stage), &p.tmap_w, fb, kt * KT::RowBytes, sg.rb * KT::TileW, pol_w);
-          bulk_load(st_sfw(stage), sfw_rb + k_off, KT::SFBytes, fb, pol_w);
+          if (p.sf_tail)
+            tma_load_3d(st_sfw(stage), &p.tmap_sfw, fb, 0, KT::KSteps * kt, sg.rb, pol_w);
+          else
+            bulk_load(st_sfw(stage), sfw_rb + k_off, KT::SFBytes, fb, pol_w);
           ++issued;
           if (++stage == S) {
             stage = 0;
@@ -514,7 +525,14 @@ inline cudaError_t launch_skinny(int M, int N, int K, const void* A, const void*
   if (e != cudaSuccess) return e;
   e = make_kmajor_tmap(&p.tmap_x, A, M, K / 2, KT::MPAD);
   if (e != cudaSuccess) return e;
-  p.kt_per_rb = K / KT::TileK;
+  p.kt_per_rb = (K + KT::TileK - 1) / KT::TileK;
+  p.sf_tail = K % KT::TileK != 0;
+  if (p.sf_tail) {
+    e = make_sf_tmap_atoms(&p.tmap_sfw, SFB, N, K, 1);
+    if (e != cudaSuccess) return e;
+    e = make_sf_tmap_atoms(&p.tmap_sfx, SFA, M, K, 1);
+    if (e != cudaSuccess) return e;
+  }
   p.units = int64_t((N + 127) / 128) * p.kt_per_rb;
   int grid = grid_cap < st->num_sms ? grid_cap : st->num_sms;
   if (p.units < grid) grid = static_cast<int>(p.units);

@@ -34,8 +34,9 @@ extern "C" {
  *   SFB : UE4M3 scale factors of B (make_layout_SFB(N, K))
  *   D   : BF16, M x N, row-major
  * plus `alpha`, the product of the two global scales (alpha = 1 reproduces the reference).
- * Shapes: M >= 1, N % 8 == 0, K % 256 == 0 (the reference also needs M % 128 == 0 and
- * N % 128 == 0).
+ * Shapes: M >= 1, N % 8 == 0, K % 32 == 0 (the reference needs M % 128 == 0, N % 128 == 0
+ * and K % 256 == 0).  With K % 64 != 0, the padding scale factors of the last K-groups must be
+ * finite (this library's quantiser writes zeros there).
  * SFA/SFB must span blackhole_sm100_sf_storage_bytes(M|N, K) bytes (rows padded to 128).
  * Pointers must be 16-byte aligned.  Errors: cudaErrorInvalidValue for a bad shape,
  * null or misaligned pointer; otherwise the launch status, as in nvfp4_gemm.hpp:594-636.

@@ -47,8 +47,9 @@ def test_sf_layout_matches_oracle(mn, k):
             assert bh.sf_offset(m, kg, k) == O.sf_offset(m, kg, k)
 
 
-@pytest.mark.parametrize("M,N,K", [(0, 128, 256), (128, 0, 256), (128, 100, 256), (128, 128, 128),
-                                   (128, 128, 320), (-1, 128, 256), (128, 4, 256), (128, 12, 256)])
+@pytest.mark.parametrize("M,N,K", [(0, 128, 256), (128, 0, 256), (128, 100, 256), (128, 128, 0),
+                                   (128, 128, 16), (128, 128, 80), (-1, 128, 256), (128, 4, 256),
+                                   (128, 12, 256)])
 def test_bad_shapes_rejected_before_launch(M, N, K):
     with pytest.raises(bh.BlackholeError) as ei:
         bh.nvfp4_bf16_gemm(M, N, K, 4096, 4096, 4096, 4096, 4096, 1.0, stream=0)

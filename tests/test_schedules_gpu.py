@@ -79,3 +79,14 @@ def test_ragged_n(schedule, M, N, K):
     """N not a multiple of 128 (only N % 8 == 0): B rows and SFB blocks past N read zeros, D
     columns past N are never written."""
     _check(M, N, K, schedule, seed=M + 7 * N + K)
+
+
+@pytest.mark.parametrize("schedule,M,N,K", [
+    ("1sm", 256, 512, 320), ("1sm", 300, 640, 1088), ("2sm", 512, 512, 576),
+    ("2sm", 640, 768, 800), ("skinny", 16, 1024, 320), ("skinny", 5, 2048, 1056),
+    ("skinny", 100, 512, 96), ("skinny", 1, 136, 32), ("auto", 1024, 1024, 2080),
+    ("auto", 300, 1000, 1888)])
+def test_k_tail(schedule, M, N, K):
+    """K not a multiple of 256 (only K % 32 == 0): the last k-tile's A/B bytes past K and its
+    scale-factor atoms past the last one read zeros."""
+    _check(M, N, K, schedule, seed=3 * M + N + K)
