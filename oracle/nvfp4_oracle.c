@@ -102,6 +102,23 @@ int64_t bho_sf_storage_bytes(int64_t MN, int64_t K) {
   return ((MN + 127) / 128) * kg_blocks * 512;
 }
 
+/* The same atom with vs-element K groups (MXFP4: vs = 32). */
+int64_t bho_sf_offset_vs(int64_t mn, int64_t kg, int64_t K, int vs) {
+  int64_t kg_blocks = (K / vs + 3) / 4;
+  return ((mn / 128) * kg_blocks + kg / 4) * 512 + (mn % 32) * 16 + ((mn / 32) % 4) * 4 +
+         (kg % 4);
+}
+
+int64_t bho_sf_storage_bytes_vs(int64_t MN, int64_t K, int vs) {
+  return ((MN + 127) / 128) * ((K / vs + 3) / 4) * 512;
+}
+
+/* UE8M0: an 8-bit biased exponent, value 2^(code - 127); code 0xFF is NaN. */
+float bho_ue8m0_to_float(uint8_t code) {
+  if (code == 0xFF) return NAN;
+  return (float)ldexp(1.0, (int)code - 127);
+}
+
 /* ------------------------------------------------------------------------------------ */
 /* Seeded normal generator: splitmix64 over a counter, Box-Muller in double.             */
 /* ------------------------------------------------------------------------------------ */
@@ -178,17 +195,52 @@ float bho_quantize_nvfp4(const float* X, int64_t rows, int64_t K, uint8_t* packe
 }
 
 /* ------------------------------------------------------------------------------------ */
+/* MXFP4 quantiser (OCP Microscaling Formats v1.0, E2M1 elements, X = 2^(floor(log2 amax) */
+/* - emax_elem)).  The exponent is read from the float's bits and the element scaling is   */
+/* a multiplication by an exact power of two, so a device quantiser reproduces it exactly. */
+/* ------------------------------------------------------------------------------------ */
+void bho_quantize_mxfp4(const float* X, int64_t rows, int64_t K, uint8_t* packed, uint8_t* sf) {
+  for (int64_t r = 0; r < rows; ++r) {
+    for (int64_t b = 0; b < K / 32; ++b) {
+      const float* x = X + r * K + b * 32;
+      float amax_b = 0.0f;
+      for (int i = 0; i < 32; ++i) {
+        float a = fabsf(x[i]);
+        if (a > amax_b) amax_b = a;
+      }
+      int ebits = (int)((f2u(amax_b) >> 23) & 0xFF); /* 0 for zero and subnormals */
+      int e = ebits == 0 ? -127 : (ebits - 127) - 2;
+      if (e < -127) e = -127;
+      if (e > 127) e = 127;
+      sf[bho_sf_offset_vs(r, b, K, 32)] = (uint8_t)(e + 127);
+      const float inv = u2f((uint32_t)(127 - e) << 23); /* 2^-e, a normal float for e <= 126 */
+      uint8_t* dst = packed + (r * K + b * 32) / 2;
+      for (int i = 0; i < 32; i += 2) {
+        uint8_t lo = bho_e2m1_from_float(x[i] * inv);
+        uint8_t hi = bho_e2m1_from_float(x[i + 1] * inv);
+        dst[i / 2] = (uint8_t)(lo | (hi << 4));
+      }
+    }
+  }
+}
+
+/* ------------------------------------------------------------------------------------ */
 /* Host reference GEMM (example/nvfp4_bf16_gemm.cu:161-168, plus alpha).                  */
 /* ------------------------------------------------------------------------------------ */
-static void dequant_row(const uint8_t* P, const uint8_t* SF, int64_t row, int64_t K,
-                        float* out) {
+static void dequant_row_fmt(int fmt, const uint8_t* P, const uint8_t* SF, int64_t row,
+                            int64_t K, float* out) {
   const uint8_t* p = P + row * (K / 2);
   for (int64_t k = 0; k < K; k += 2) {
     uint8_t byte = p[k / 2];
-    float s = bho_ue4m3_to_float(SF[bho_sf_offset(row, k / 16, K)]);
+    float s = fmt == 1 ? bho_ue8m0_to_float(SF[bho_sf_offset_vs(row, k / 32, K, 32)])
+                       : bho_ue4m3_to_float(SF[bho_sf_offset(row, k / 16, K)]);
     out[k] = bho_e2m1_to_float(byte & 0xF) * s;
     out[k + 1] = bho_e2m1_to_float(byte >> 4) * s;
   }
+}
+static void dequant_row(const uint8_t* P, const uint8_t* SF, int64_t row, int64_t K,
+                        float* out) {
+  dequant_row_fmt(0, P, SF, row, K, out);
 }
 
 static float dot_seq(const float* a, const float* b, int64_t K, double* absdot) {
@@ -215,6 +267,7 @@ typedef struct {
   int64_t S;
   const int64_t *ms, *ns;
   int sampled;
+  int fmt;
 } gemm_job;
 
 static void* gemm_worker(void* arg) {
@@ -222,7 +275,7 @@ static void* gemm_worker(void* arg) {
   float* arow = (float*)malloc(sizeof(float) * (size_t)j->K);
   if (!j->sampled) {
     for (int64_t m = j->m0; m < j->m1; ++m) {
-      dequant_row(j->A, j->SFA, m, j->K, arow);
+      dequant_row_fmt(j->fmt, j->A, j->SFA, m, j->K, arow);
       for (int64_t n = 0; n < j->N; ++n) {
         double ad;
         float acc = dot_seq(arow, j->Bdq + n * j->K, j->K, &ad);
@@ -233,8 +286,8 @@ static void* gemm_worker(void* arg) {
   } else {
     float* brow = (float*)malloc(sizeof(float) * (size_t)j->K);
     for (int64_t s = j->m0; s < j->m1; ++s) {
-      dequant_row(j->A, j->SFA, j->ms[s], j->K, arow);
-      dequant_row(j->B, j->SFB, j->ns[s], j->K, brow);
+      dequant_row_fmt(j->fmt, j->A, j->SFA, j->ms[s], j->K, arow);
+      dequant_row_fmt(j->fmt, j->B, j->SFB, j->ns[s], j->K, brow);
       double ad;
       float acc = dot_seq(arow, brow, j->K, &ad);
       j->D[s] = bho_bf16_from_float(j->alpha * acc);
@@ -269,23 +322,25 @@ typedef struct {
   const uint8_t *P, *SF;
   int64_t K, r0, r1;
   float* out;
+  int fmt;
 } dequant_job;
 
 static void* dequant_worker(void* arg) {
   dequant_job* j = (dequant_job*)arg;
-  for (int64_t r = j->r0; r < j->r1; ++r) dequant_row(j->P, j->SF, r, j->K, j->out + r * j->K);
+  for (int64_t r = j->r0; r < j->r1; ++r)
+    dequant_row_fmt(j->fmt, j->P, j->SF, r, j->K, j->out + r * j->K);
   return NULL;
 }
 
-static void dequant_rows_parallel(const uint8_t* P, const uint8_t* SF, int64_t rows, int64_t K,
-                                  float* out, int nthreads) {
+static void dequant_rows_parallel(int fmt, const uint8_t* P, const uint8_t* SF, int64_t rows,
+                                  int64_t K, float* out, int nthreads) {
   if (nthreads < 1) nthreads = 1;
   if (nthreads > 256) nthreads = 256;
   if (nthreads > rows) nthreads = (int)(rows > 0 ? rows : 1);
   pthread_t tid[256];
   dequant_job jobs[256];
   for (int t = 0; t < nthreads; ++t) {
-    dequant_job j = {P, SF, K, rows * t / nthreads, rows * (t + 1) / nthreads, out};
+    dequant_job j = {P, SF, K, rows * t / nthreads, rows * (t + 1) / nthreads, out, fmt};
     jobs[t] = j;
   }
   if (nthreads == 1) {
@@ -296,22 +351,36 @@ static void dequant_rows_parallel(const uint8_t* P, const uint8_t* SF, int64_t r
   for (int t = 0; t < nthreads; ++t) pthread_join(tid[t], NULL);
 }
 
+void bho_gemm_ref_full_fmt(int fmt, int64_t M, int64_t N, int64_t K, const uint8_t* A,
+                           const uint8_t* SFA, const uint8_t* B, const uint8_t* SFB, float alpha,
+                           uint16_t* D, double* absdot, int nthreads) {
+  float* Bdq = (float*)malloc(sizeof(float) * (size_t)(N * K));
+  dequant_rows_parallel(fmt, B, SFB, N, K, Bdq, nthreads);
+  gemm_job job = {M, N, K, A, SFA, B, SFB, alpha, D, absdot, Bdq, 0, 0, 0, NULL, NULL, 0, fmt};
+  run_jobs(&job, M, nthreads);
+  free(Bdq);
+}
+
+void bho_gemm_ref_sampled_fmt(int fmt, int64_t M, int64_t N, int64_t K, const uint8_t* A,
+                              const uint8_t* SFA, const uint8_t* B, const uint8_t* SFB,
+                              float alpha, int64_t S, const int64_t* ms, const int64_t* ns,
+                              uint16_t* D_out, double* absdot, int nthreads) {
+  gemm_job job = {M, N, K, A, SFA, B, SFB, alpha, D_out, absdot, NULL, 0, 0, S, ms, ns, 1, fmt};
+  run_jobs(&job, S, nthreads);
+}
+
 void bho_gemm_ref_full(int64_t M, int64_t N, int64_t K, const uint8_t* A, const uint8_t* SFA,
                        const uint8_t* B, const uint8_t* SFB, float alpha, uint16_t* D,
                        double* absdot, int nthreads) {
-  float* Bdq = (float*)malloc(sizeof(float) * (size_t)(N * K));
-  dequant_rows_parallel(B, SFB, N, K, Bdq, nthreads);
-  gemm_job job = {M, N, K, A, SFA, B, SFB, alpha, D, absdot, Bdq, 0, 0, 0, NULL, NULL, 0};
-  run_jobs(&job, M, nthreads);
-  free(Bdq);
+  bho_gemm_ref_full_fmt(0, M, N, K, A, SFA, B, SFB, alpha, D, absdot, nthreads);
 }
 
 void bho_gemm_ref_sampled(int64_t M, int64_t N, int64_t K, const uint8_t* A,
                           const uint8_t* SFA, const uint8_t* B, const uint8_t* SFB,
                           float alpha, int64_t S, const int64_t* ms, const int64_t* ns,
                           uint16_t* D_out, double* absdot, int nthreads) {
-  gemm_job job = {M, N, K, A, SFA, B, SFB, alpha, D_out, absdot, NULL, 0, 0, S, ms, ns, 1};
-  run_jobs(&job, S, nthreads);
+  bho_gemm_ref_sampled_fmt(0, M, N, K, A, SFA, B, SFB, alpha, S, ms, ns, D_out, absdot,
+                           nthreads);
 }
 
 double bho_tolerance(float ref, float got, float alpha, int64_t K, double absdot) {

@@ -74,6 +74,28 @@ void bho_gemm_ref_sampled(int64_t M, int64_t N, int64_t K, const uint8_t* A,
                           float alpha, int64_t S, const int64_t* ms, const int64_t* ns,
                           uint16_t* D_out, double* absdot, int nthreads);
 
+/* ---- MXFP4 (OCP MX v1.0: E2M1 elements, one UE8M0 scale per 32 along K) ------------ */
+/* Not part of the reference; the sibling format served behind the same operator.  The
+ * scale-factor layout is the same 128x4 blocked layout with 32-element K groups (CUTLASS
+ * Sm1xxBlockScaledConfig<32>); tests/golden/make_golden_mx.cpp pins it and the decode. */
+float   bho_ue8m0_to_float(uint8_t code);  /* 2^(code-127); 0xFF -> NaN */
+/* Layout with `vs`-element K groups (vs = 16: NVFP4, vs = 32: MXFP4). */
+int64_t bho_sf_offset_vs(int64_t mn, int64_t kg, int64_t K, int vs);
+int64_t bho_sf_storage_bytes_vs(int64_t MN, int64_t K, int vs);
+/* Per 32-block b: shared exponent e_b = floor(log2(amax_b)) - 2 (2 = emax of E2M1), clamped
+ * to [-127, 127] (amax_b subnormal or 0 -> -127); scale code = e_b + 127; element code =
+ * e2m1(x * 2^-e_b) (exact scaling, RNE, saturating to 6).  K % 32 == 0; sf zero-filled
+ * first by the caller. */
+void bho_quantize_mxfp4(const float* X, int64_t rows, int64_t K, uint8_t* packed, uint8_t* sf);
+/* The reference GEMM for a format: fmt 0 = NVFP4 (as above), 1 = MXFP4. */
+void bho_gemm_ref_full_fmt(int fmt, int64_t M, int64_t N, int64_t K, const uint8_t* A,
+                           const uint8_t* SFA, const uint8_t* B, const uint8_t* SFB, float alpha,
+                           uint16_t* D, double* absdot, int nthreads);
+void bho_gemm_ref_sampled_fmt(int fmt, int64_t M, int64_t N, int64_t K, const uint8_t* A,
+                              const uint8_t* SFA, const uint8_t* B, const uint8_t* SFB,
+                              float alpha, int64_t S, const int64_t* ms, const int64_t* ns,
+                              uint16_t* D_out, double* absdot, int nthreads);
+
 /* Tolerance bound for one element:
  *   ulp_bf16(max(|ref|,|got|)) + |alpha| * K * 2^-24 * absdot
  * i.e. one BF16 ulp of the output plus the worst-case FP32 reassociation error of a

@@ -64,6 +64,21 @@ def lib():
         L.bho_gemm_ref_sampled.argtypes = [c_i64, c_i64, c_i64, c_ptr, c_ptr, c_ptr, c_ptr,
                                            ctypes.c_float, c_i64, c_ptr, c_ptr, c_ptr, c_ptr,
                                            ctypes.c_int]
+        L.bho_ue8m0_to_float.restype = ctypes.c_float
+        L.bho_ue8m0_to_float.argtypes = [ctypes.c_uint8]
+        L.bho_sf_offset_vs.restype = c_i64
+        L.bho_sf_offset_vs.argtypes = [c_i64, c_i64, c_i64, ctypes.c_int]
+        L.bho_sf_storage_bytes_vs.restype = c_i64
+        L.bho_sf_storage_bytes_vs.argtypes = [c_i64, c_i64, ctypes.c_int]
+        L.bho_quantize_mxfp4.restype = None
+        L.bho_quantize_mxfp4.argtypes = [c_ptr, c_i64, c_i64, c_ptr, c_ptr]
+        L.bho_gemm_ref_full_fmt.restype = None
+        L.bho_gemm_ref_full_fmt.argtypes = [ctypes.c_int, c_i64, c_i64, c_i64, c_ptr, c_ptr, c_ptr,
+                                            c_ptr, ctypes.c_float, c_ptr, c_ptr, ctypes.c_int]
+        L.bho_gemm_ref_sampled_fmt.restype = None
+        L.bho_gemm_ref_sampled_fmt.argtypes = [ctypes.c_int, c_i64, c_i64, c_i64, c_ptr, c_ptr,
+                                               c_ptr, c_ptr, ctypes.c_float, c_i64, c_ptr, c_ptr,
+                                               c_ptr, c_ptr, ctypes.c_int]
         L.bho_tolerance.restype = ctypes.c_double
         L.bho_tolerance.argtypes = [ctypes.c_float, ctypes.c_float, ctypes.c_float, c_i64, ctypes.c_double]
         _lib = L
@@ -132,25 +147,46 @@ def quantize(X: np.ndarray):
     return packed, sf, float(g)
 
 
-def gemm_full(M, N, K, A, SFA, B, SFB, alpha=1.0, nthreads=0, want_absdot=True):
+FORMATS = {"nvfp4": 0, "mxfp4": 1}
+
+
+def sf_storage_bytes_vs(mn: int, k: int, vs: int) -> int:
+    return int(lib().bho_sf_storage_bytes_vs(mn, k, vs))
+
+
+def sf_offset_vs(mn: int, kg: int, k: int, vs: int) -> int:
+    return int(lib().bho_sf_offset_vs(mn, kg, k, vs))
+
+
+def quantize_mxfp4(X: np.ndarray):
+    """MXFP4-quantise a (rows, K) float32 matrix (K % 32 == 0): returns (packed u8, sf u8)."""
+    X = np.ascontiguousarray(X, dtype=np.float32)
+    rows, k = X.shape
+    packed = np.zeros(rows * k // 2, dtype=np.uint8)
+    sf = np.zeros(sf_storage_bytes_vs(rows, k, 32), dtype=np.uint8)
+    lib().bho_quantize_mxfp4(_p(X), rows, k, _p(packed), _p(sf))
+    return packed, sf
+
+
+def gemm_full(M, N, K, A, SFA, B, SFB, alpha=1.0, nthreads=0, want_absdot=True, fmt="nvfp4"):
     """Full host reference: returns (D bf16 bits as uint16 [M,N], absdot [M,N] or None)."""
     D = np.empty((M, N), dtype=np.uint16)
     ad = np.empty((M, N), dtype=np.float64) if want_absdot else None
     nt = nthreads if nthreads > 0 else (os.cpu_count() or 1)
-    lib().bho_gemm_ref_full(M, N, K, _p(A), _p(SFA), _p(B), _p(SFB), alpha, _p(D),
-                            _p(ad) if ad is not None else None, nt)
+    lib().bho_gemm_ref_full_fmt(FORMATS[fmt], M, N, K, _p(A), _p(SFA), _p(B), _p(SFB), alpha,
+                                _p(D), _p(ad) if ad is not None else None, nt)
     return D, ad
 
 
-def gemm_sampled(M, N, K, A, SFA, B, SFB, ms, ns, alpha=1.0, nthreads=0):
+def gemm_sampled(M, N, K, A, SFA, B, SFB, ms, ns, alpha=1.0, nthreads=0, fmt="nvfp4"):
     ms = np.ascontiguousarray(ms, dtype=np.int64)
     ns = np.ascontiguousarray(ns, dtype=np.int64)
     S = ms.size
     D = np.empty(S, dtype=np.uint16)
     ad = np.empty(S, dtype=np.float64)
     nt = nthreads if nthreads > 0 else (os.cpu_count() or 1)
-    lib().bho_gemm_ref_sampled(M, N, K, _p(A), _p(SFA), _p(B), _p(SFB), alpha, S,
-                               _p(ms), _p(ns), _p(D), _p(ad), nt)
+    lib().bho_gemm_ref_sampled_fmt(FORMATS[fmt], M, N, K, _p(A), _p(SFA), _p(B), _p(SFB),
+                                   alpha, S, _p(ms), _p(ns), _p(D), _p(ad), nt)
     return D, ad
 
 
