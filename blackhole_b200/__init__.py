@@ -17,6 +17,8 @@ __all__ = [
     "LIB_PATH", "load", "nvfp4_bf16_gemm", "sf_storage_bytes", "sf_offset",
     "device_status", "BlackholeError", "nvfp4_quantize", "quantize_tensor",
     "nvfp4_bf16_gemm_ex", "workspace_bytes", "SCHEDULES", "nvfp4_bf16_gemm_noalloc",
+    "selftest_bounded_wait", "mxfp4_bf16_gemm", "mxfp4_sf_storage_bytes", "mxfp4_quantize",
+    "quantize_tensor_mxfp4",
 ]
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -56,6 +58,15 @@ def load():
     L.blackhole_sm100_nvfp4_bf16_gemm_noalloc.restype = i32
     L.blackhole_sm100_nvfp4_bf16_gemm_noalloc.argtypes = [i32, i32, i32, vp, vp, vp, vp, vp,
                                                           ctypes.c_float, vp]
+    L.blackhole_sm100_mxfp4_bf16_gemm.restype = i32
+    L.blackhole_sm100_mxfp4_bf16_gemm.argtypes = [i32, i32, i32, vp, vp, vp, vp, vp, ctypes.c_float, vp]
+    L.blackhole_sm100_mxfp4_bf16_gemm_ex.restype = i32
+    L.blackhole_sm100_mxfp4_bf16_gemm_ex.argtypes = [i32, i32, i32, vp, vp, vp, vp, vp, ctypes.c_float,
+                                                     i32, vp, i64, vp]
+    L.blackhole_sm100_mxfp4_sf_storage_bytes.restype = i64
+    L.blackhole_sm100_mxfp4_sf_storage_bytes.argtypes = [i64, i64]
+    L.blackhole_sm100_mxfp4_quantize.restype = i32
+    L.blackhole_sm100_mxfp4_quantize.argtypes = [vp, i32, i32, i32, vp, vp, vp]
     L.blackhole_sm100_workspace_bytes.restype = i64
     L.blackhole_sm100_workspace_bytes.argtypes = [i32, i32, i32]
     L.blackhole_sm100_sf_storage_bytes.restype = i64
@@ -133,6 +144,47 @@ def nvfp4_bf16_gemm_ex(M: int, N: int, K: int, A, SFA, B, SFB, D, alpha: float =
         int(workspace_bytes), _stream(stream))
     if rc != 0:
         raise BlackholeError("blackhole_sm100_nvfp4_bf16_gemm_ex", rc)
+
+
+def mxfp4_bf16_gemm(M: int, N: int, K: int, A, SFA, B, SFB, D, alpha: float = 1.0, stream=None,
+                    schedule: str = "auto", workspace=None, workspace_bytes: int = 0) -> None:
+    """D = bf16(alpha * A . B^T) for MXFP4 operands (E2M1, one UE8M0 scale per 32 elements
+    along K, 128x4 layout with 32-element groups: mxfp4_sf_storage_bytes(M|N, K) bytes).
+    Same shapes, schedules and errors as nvfp4_bf16_gemm_ex."""
+    if workspace is not None and hasattr(workspace, "numel") and not workspace_bytes:
+        workspace_bytes = workspace.numel() * workspace.element_size()
+    rc = load().blackhole_sm100_mxfp4_bf16_gemm_ex(
+        int(M), int(N), int(K), _ptr(A), _ptr(SFA), _ptr(B), _ptr(SFB), _ptr(D), float(alpha),
+        SCHEDULES[schedule], _ptr(workspace) if workspace is not None else None,
+        int(workspace_bytes), _stream(stream))
+    if rc != 0:
+        raise BlackholeError("blackhole_sm100_mxfp4_bf16_gemm_ex", rc)
+
+
+def mxfp4_sf_storage_bytes(mn: int, k: int) -> int:
+    """Bytes of an (mn x k) MXFP4 scale-factor tensor (padding included)."""
+    return int(load().blackhole_sm100_mxfp4_sf_storage_bytes(int(mn), int(k)))
+
+
+def mxfp4_quantize(X, rows: int, K: int, packed, sf, x_is_bf16: bool = False, stream=None) -> None:
+    """Quantise X (rows x K, FP32 or BF16, K % 32 == 0) to MXFP4 on the GPU (asynchronous)."""
+    rc = load().blackhole_sm100_mxfp4_quantize(
+        _ptr(X), 1 if x_is_bf16 else 0, int(rows), int(K), _ptr(packed), _ptr(sf), _stream(stream))
+    if rc != 0:
+        raise BlackholeError("blackhole_sm100_mxfp4_quantize", rc)
+
+
+def quantize_tensor_mxfp4(X, stream=None):
+    """MXFP4 version of quantize_tensor: returns (packed uint8 [rows, K/2], sf uint8)."""
+    import torch
+
+    if X.dim() != 2 or X.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("X must be a 2-D float32 or bfloat16 tensor")
+    rows, K = X.shape
+    packed = torch.empty((rows, K // 2), dtype=torch.uint8, device=X.device)
+    sf = torch.empty(mxfp4_sf_storage_bytes(rows, K), dtype=torch.uint8, device=X.device)
+    mxfp4_quantize(X, rows, K, packed, sf, x_is_bf16=(X.dtype == torch.bfloat16), stream=stream)
+    return packed, sf
 
 
 def nvfp4_bf16_gemm_noalloc(M: int, N: int, K: int, A, SFA, B, SFB, D, alpha: float = 1.0,

@@ -77,6 +77,34 @@ int blackhole_sm100_nvfp4_bf16_gemm_ex(int M, int N, int K, const void* A, const
       workspace, workspace_bytes, stream));
 }
 
+int blackhole_sm100_mxfp4_bf16_gemm(int M, int N, int K, const void* A, const void* SFA,
+                                    const void* B, const void* SFB, void* D, float alpha,
+                                    cudaStream_t stream) {
+  return static_cast<int>(
+      blackhole::sm100::mxfp4_bf16_gemm(M, N, K, A, SFA, B, SFB, D, alpha, stream));
+}
+
+int blackhole_sm100_mxfp4_bf16_gemm_ex(int M, int N, int K, const void* A, const void* SFA,
+                                       const void* B, const void* SFB, void* D, float alpha,
+                                       int schedule, void* workspace, int64_t workspace_bytes,
+                                       cudaStream_t stream) {
+  if (schedule < 0 || schedule > 4) return static_cast<int>(cudaErrorInvalidValue);
+  return static_cast<int>(blackhole::sm100::mxfp4_bf16_gemm_ex(
+      M, N, K, A, SFA, B, SFB, D, alpha, static_cast<blackhole::sm100::Nvfp4Schedule>(schedule),
+      workspace, workspace_bytes, stream));
+}
+
+int64_t blackhole_sm100_mxfp4_sf_storage_bytes(int64_t mn, int64_t k) {
+  if (mn < 0 || k < 0) return -1;
+  return blackhole::sf_storage_bytes_vs(mn, k, 32);
+}
+
+int blackhole_sm100_mxfp4_quantize(const void* X, int x_is_bf16, int rows, int K, void* packed,
+                                   void* sf, cudaStream_t stream) {
+  return static_cast<int>(
+      blackhole::sm100::mxfp4_quantize(X, x_is_bf16, rows, K, packed, sf, stream));
+}
+
 int64_t blackhole_sm100_workspace_bytes(int M, int N, int K) {
   if (M < 1 || N < 1 || K < 1) return -1;
   if (M > 128) return 0;

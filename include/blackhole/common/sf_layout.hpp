@@ -46,6 +46,19 @@ BLACKHOLE_HD constexpr int64_t sf_storage_bytes(int64_t mn, int64_t k) {
   return ((mn + kSfAtomRows - 1) / kSfAtomRows) * sf_k_atoms(k) * kSfAtomBytes;
 }
 
+// The same layout with `vs`-element K groups (vs = 16: NVFP4; vs = 32: MXFP4, one UE8M0 byte
+// per 32 elements -- CUTLASS Sm1xxBlockScaledConfig<32>).  An atom then covers 128 K-elements.
+BLACKHOLE_HD constexpr int64_t sf_k_atoms_vs(int64_t k, int vs) {
+  return (k / vs + kSfAtomGroups - 1) / kSfAtomGroups;
+}
+BLACKHOLE_HD constexpr int64_t sf_offset_vs(int64_t mn, int64_t kg, int64_t k, int vs) {
+  return ((mn / kSfAtomRows) * sf_k_atoms_vs(k, vs) + kg / kSfAtomGroups) * kSfAtomBytes +
+         (mn % 32) * 16 + ((mn / 32) % 4) * 4 + (kg % kSfAtomGroups);
+}
+BLACKHOLE_HD constexpr int64_t sf_storage_bytes_vs(int64_t mn, int64_t k, int vs) {
+  return ((mn + kSfAtomRows - 1) / kSfAtomRows) * sf_k_atoms_vs(k, vs) * kSfAtomBytes;
+}
+
 // Byte offset of the atom holding rows [128*row_block, +128) and K-groups [4*k_atom, +4).
 BLACKHOLE_HD constexpr int64_t sf_atom_offset(int64_t row_block, int64_t k_atom, int64_t k) {
   return (row_block * sf_k_atoms(k) + k_atom) * kSfAtomBytes;

@@ -94,12 +94,13 @@ inline cudaError_t library_workspace(int dev, cudaStream_t stream, int64_t bytes
 
 }  // namespace detail
 
-// Full control: schedule choice and (for the skinny schedule) a caller-owned workspace.
-// workspace == nullptr selects the library-owned workspace.
-inline cudaError_t nvfp4_bf16_gemm_ex(int M, int N, int K, void const* A, void const* SFA,
-                                      void const* B, void const* SFB, void* D, float alpha,
-                                      Nvfp4Schedule schedule, void* workspace,
-                                      int64_t workspace_bytes, cudaStream_t stream) {
+// Full control: element format, schedule choice and (for the skinny schedule) a caller-owned
+// workspace.  workspace == nullptr selects the library-owned workspace.
+template <class Fmt>
+inline cudaError_t block_scaled_bf16_gemm_ex(int M, int N, int K, void const* A, void const* SFA,
+                                             void const* B, void const* SFB, void* D, float alpha,
+                                             Nvfp4Schedule schedule, void* workspace,
+                                             int64_t workspace_bytes, cudaStream_t stream) {
   cudaError_t e = nvfp4_check_args(M, N, K, A, SFA, B, SFB, D);
   if (e != cudaSuccess) return e;
   detail::DeviceState* st = detail::prepare_device();
@@ -114,9 +115,11 @@ inline cudaError_t nvfp4_bf16_gemm_ex(int M, int N, int K, void const* A, void c
                           : Nvfp4Schedule::kTwoSm;
   switch (schedule) {
     case Nvfp4Schedule::kOneSm:
-      return detail::launch_1sm<Nvfp4GemmTraits>(M, N, K, A, SFA, B, SFB, D, alpha, st, dev, stream);
+      return detail::launch_1sm<Nvfp4GemmTraitsT<256, 4, Fmt>>(M, N, K, A, SFA, B, SFB, D, alpha,
+                                                                st, dev, stream);
     case Nvfp4Schedule::kTwoSm:
-      return detail::launch_2sm<Nvfp4Gemm2SmTraits>(M, N, K, A, SFA, B, SFB, D, alpha, st, dev, stream);
+      return detail::launch_2sm<Nvfp4Gemm2SmTraitsT<256, 5, Fmt>>(M, N, K, A, SFA, B, SFB, D,
+                                                                   alpha, st, dev, stream);
     case Nvfp4Schedule::kSkinny:
     case Nvfp4Schedule::kSkinnyNoPrefetch: {
       if (M > 128) return cudaErrorInvalidValue;
@@ -126,12 +129,38 @@ inline cudaError_t nvfp4_bf16_gemm_ex(int M, int N, int K, void const* A, void c
         if (e != cudaSuccess) return e;
         workspace_bytes = need;
       }
-      return nvfp4_bf16_gemm_skinny(M, N, K, A, SFA, B, SFB, D, alpha, workspace, workspace_bytes,
-                                    stream, 1 << 30, schedule == Nvfp4Schedule::kSkinny);
+      return block_scaled_bf16_gemm_skinny<Fmt>(M, N, K, A, SFA, B, SFB, D, alpha, workspace,
+                                                workspace_bytes, stream, 1 << 30,
+                                                schedule == Nvfp4Schedule::kSkinny);
     }
     default:
       return cudaErrorInvalidValue;
   }
+}
+
+inline cudaError_t nvfp4_bf16_gemm_ex(int M, int N, int K, void const* A, void const* SFA,
+                                      void const* B, void const* SFB, void* D, float alpha,
+                                      Nvfp4Schedule schedule, void* workspace,
+                                      int64_t workspace_bytes, cudaStream_t stream) {
+  return block_scaled_bf16_gemm_ex<Nvfp4Format>(M, N, K, A, SFA, B, SFB, D, alpha, schedule,
+                                                workspace, workspace_bytes, stream);
+}
+
+// MXFP4 (OCP MX: E2M1 elements, one UE8M0 scale per 32 along K, same 128x4 layout with
+// 32-element groups: sf_storage_bytes_vs(MN, K, 32) bytes); not in the reference, served by
+// the same schedules.  Shapes as nvfp4_bf16_gemm.
+inline cudaError_t mxfp4_bf16_gemm_ex(int M, int N, int K, void const* A, void const* SFA,
+                                      void const* B, void const* SFB, void* D, float alpha,
+                                      Nvfp4Schedule schedule, void* workspace,
+                                      int64_t workspace_bytes, cudaStream_t stream) {
+  return block_scaled_bf16_gemm_ex<Mxfp4Format>(M, N, K, A, SFA, B, SFB, D, alpha, schedule,
+                                                workspace, workspace_bytes, stream);
+}
+inline cudaError_t mxfp4_bf16_gemm(int M, int N, int K, void const* A, void const* SFA,
+                                   void const* B, void const* SFB, void* D, float alpha = 1.0f,
+                                   cudaStream_t stream = nullptr) {
+  return mxfp4_bf16_gemm_ex(M, N, K, A, SFA, B, SFB, D, alpha, Nvfp4Schedule::kAuto, nullptr, 0,
+                            stream);
 }
 
 //   A_packed : E2M1, M x K, K-contiguous (two per byte, low nibble first)

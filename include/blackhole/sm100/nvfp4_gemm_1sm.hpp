@@ -18,6 +18,7 @@
 // Used for small problems; large ones take the two-SM schedule (nvfp4_gemm_2sm.hpp).
 // =====================================================================================
 
+#include <blackhole/sm100/block_scale_format.hpp>
 #include <blackhole/sm100/nvfp4_gemm_common.hpp>
 
 namespace blackhole::sm100 {
@@ -25,9 +26,10 @@ namespace blackhole::sm100 {
 // =====================================================================================
 // 1. Compile-time configuration
 // =====================================================================================
-template <int TileK_ = 256, int Stages_ = 4>
+template <int TileK_ = 256, int Stages_ = 4, class Fmt_ = Nvfp4Format>
 struct Nvfp4GemmTraitsT {
-  static constexpr int SFVecSize = kNvfp4SfVec;  // 16 elements per scale factor
+  using Fmt = Fmt_;
+  static constexpr int SFVecSize = Fmt::SfVec;   // elements per scale factor (16 or 32)
 
   static constexpr int TileM = 128;              // UMMA M (one CTA, TMEM lanes)
   static constexpr int TileN = 256;              // UMMA N
@@ -39,8 +41,12 @@ struct Nvfp4GemmTraitsT {
   static constexpr int RowBytes = TileK / 2;                        // 128 or 64
   static constexpr int ABytes = TileM * RowBytes;                   // 16 KB
   static constexpr int BBytes = TileN * RowBytes;                   // 32 KB
-  static constexpr int SFABytes = (TileM / 128) * KSteps * 512;     // 2 KB
-  static constexpr int SFBBytes = (TileN / 128) * KSteps * 512;     // 4 KB
+  // 512-byte scale-factor atoms per 128 rows and k-tile: 4 (NVFP4) or 2 (MXFP4); k-step j
+  // reads atom j / StepsPerAtom at byte pair 2 * (j % StepsPerAtom) of each entry.
+  static constexpr int StepsPerAtom = SFVecSize / 16;
+  static constexpr int SfAtoms = KSteps / StepsPerAtom;
+  static constexpr int SFABytes = (TileM / 128) * SfAtoms * 512;    // 2 KB (NVFP4)
+  static constexpr int SFBBytes = (TileN / 128) * SfAtoms * 512;    // 4 KB (NVFP4)
   static constexpr int StageBytes = ABytes + BBytes + SFABytes + SFBBytes;
 
   static constexpr int NumWarps = 10;
@@ -55,7 +61,7 @@ struct Nvfp4GemmTraitsT {
   static constexpr uint32_t TmemCols = 512;
   static constexpr uint32_t AccCol = 0;
   static constexpr uint32_t SfCol = 256;
-  static constexpr uint32_t SfStride = 12 * KSteps;
+  static constexpr uint32_t SfStride = 12 * SfAtoms;
 
   // epilogue staging: one 32-row x 16-column BF16 box (1 KB, 32B-swizzled) per epilogue warp
   static constexpr int StoreBoxBytes = 32 * 16 * 2;
@@ -205,11 +211,11 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
                       pol_a);
           tma_load_2d(sB + stage * KT::BBytes, &p.tmap_b, fb, kt * KT::RowBytes, n_blk * KT::TileN,
                       pol_b);
-          const int64_t k_off = int64_t(kt) * KT::KSteps * 512;
+          const int64_t k_off = int64_t(kt) * KT::SfAtoms * 512;
           if (p.sf_tail) {  // atoms past K (and blocks past N) read zeros
-            tma_load_3d(sSFA + stage * KT::SFABytes, &p.tmap_sfa, fb, 0, KT::KSteps * kt, m_blk,
+            tma_load_3d(sSFA + stage * KT::SFABytes, &p.tmap_sfa, fb, 0, KT::SfAtoms * kt, m_blk,
                         pol_a);
-            tma_load_3d(sSFB + stage * KT::SFBBytes, &p.tmap_sfb, fb, 0, KT::KSteps * kt,
+            tma_load_3d(sSFB + stage * KT::SFBBytes, &p.tmap_sfb, fb, 0, KT::SfAtoms * kt,
                         2 * n_blk, pol_b);
           } else {
             bulk_load(sSFA + stage * KT::SFABytes, sfa_src + k_off, KT::SFABytes, fb, pol_a);
@@ -239,7 +245,7 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
     // ------------------------------ MMA issuer --------------------------------------
     // Per k-tile: probe the next stage's barrier, copy this stage's scale factors to TMEM,
     // four MMAs, commit, then consume the probe (falling back to a bounded wait).
-    constexpr uint32_t idesc = idesc_nvf4(KT::TileM, KT::TileN);
+    constexpr uint32_t idesc = idesc_bs(KT::TileM, KT::TileN, KT::Fmt::ScaleType);
     int stage = 0;
     uint32_t phase = 0;
     uint32_t acc_phase = 0;
@@ -251,10 +257,10 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
       const uint32_t sfb_s = sSFB + st * KT::SFBBytes;
       const uint32_t ta = tmem + KT::SfCol + KT::SfStride * b;
 #pragma unroll
-      for (int j = 0; j < KT::KSteps; ++j) {
+      for (int j = 0; j < KT::SfAtoms; ++j) {
         tc_cp_32x128b_warpx4_w(ta + 4 * j, desc_sf_atom(sfa_s + 512 * j));
-        tc_cp_32x128b_warpx4_w(ta + 4 * KT::KSteps + 8 * j, desc_sf_atom(sfb_s + 512 * j));
-        tc_cp_32x128b_warpx4_w(ta + 4 * KT::KSteps + 8 * j + 4,
+        tc_cp_32x128b_warpx4_w(ta + 4 * KT::SfAtoms + 8 * j, desc_sf_atom(sfb_s + 512 * j));
+        tc_cp_32x128b_warpx4_w(ta + 4 * KT::SfAtoms + 8 * j + 4,
                                desc_sf_atom(sfb_s + KT::SFBBytes / 2 + 512 * j));
       }
     };
@@ -282,8 +288,12 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
 #pragma unroll
         for (int j = 0; j < KT::KSteps; ++j) {
           // +32 bytes of K per step inside the swizzled row (descriptor units: 16 B)
-          tc_mma_nvf4_w(tmem + KT::AccCol, adesc + 2 * j, bdesc + 2 * j, idesc, ta + 4 * j,
-                        ta + 4 * KT::KSteps + 8 * j, (kt | j) != 0 ? 1u : 0u);
+          const int at = j / KT::StepsPerAtom;
+          const uint32_t sid = 2u * uint32_t(j % KT::StepsPerAtom);   // byte in the entry
+          tc_mma_nvf4_w<KT::SFVecSize>(
+              tmem + KT::AccCol, adesc + 2 * j, bdesc + 2 * j, idesc_with_sf_id(idesc, sid),
+              sf_tmem_addr(ta + 4 * at, sid), sf_tmem_addr(ta + 4 * KT::SfAtoms + 8 * at, sid),
+              (kt | j) != 0 ? 1u : 0u);
         }
         tc_commit_w(empty_bar(stage));
         issued_any = true;
@@ -411,14 +421,13 @@ inline cudaError_t launch_1sm(int M, int N, int K, const void* A, const void* SF
   p.tiles_n = (N + KT::TileN - 1) / KT::TileN;
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.k_tiles = (K + KT::TileK - 1) / KT::TileK;
-  p.sf_k_atoms = static_cast<int>(sf_k_atoms(K));
+  p.sf_k_atoms = static_cast<int>(sf_k_atoms_vs(K, KT::SFVecSize));
   p.n_blocks128 = (N + 127) / 128;
   p.sf_tail = K % KT::TileK != 0;
   if (p.sf_tail) {
-    if (KT::KSteps != 4) return cudaErrorInvalidValue;  // the tail maps fetch 4 atoms per k-tile
-    e = make_sf_tmap_atoms(&p.tmap_sfa, SFA, M, K, 1);
+    e = make_sf_tmap_atoms(&p.tmap_sfa, SFA, M, K, 1, KT::SfAtoms, KT::SFVecSize);
     if (e != cudaSuccess) return e;
-    e = make_sf_tmap_atoms(&p.tmap_sfb, SFB, N, K, 2);
+    e = make_sf_tmap_atoms(&p.tmap_sfb, SFB, N, K, 2, KT::SfAtoms, KT::SFVecSize);
     if (e != cudaSuccess) return e;
   }
   const int grid = p.num_tiles < st->num_sms ? p.num_tiles : st->num_sms;

@@ -28,12 +28,15 @@
 // rows per block they cost ~20% of the mainloop; as 2 KB rows ~10%).
 // =====================================================================================
 
+#include <blackhole/sm100/block_scale_format.hpp>
 #include <blackhole/sm100/nvfp4_gemm_common.hpp>
 
 namespace blackhole::sm100 {
 
-template <int TileK_ = 256, int Stages_ = 5>
+template <int TileK_ = 256, int Stages_ = 5, class Fmt_ = Nvfp4Format>
 struct Nvfp4Gemm2SmTraitsT {
+  using Fmt = Fmt_;
+  static constexpr int SFVecSize = Fmt::SfVec;
   static constexpr int TileM = 256;              // per pair (UMMA M)
   static constexpr int CtaM = 128;
   static constexpr int TileN = 256;              // UMMA N
@@ -45,8 +48,11 @@ struct Nvfp4Gemm2SmTraitsT {
   static constexpr int RowBytes = TileK / 2;
   static constexpr int ABytes = CtaM * RowBytes;           // 16 KB
   static constexpr int BBytes = CtaN * RowBytes;           // 16 KB
-  static constexpr int SFABytes = KSteps * 512;            // 2 KB (own 128 rows)
-  static constexpr int SFBBytes = 2 * KSteps * 512;        // 4 KB (all 256 rows)
+  // scale-factor atoms per 128 rows and k-tile: 4 (NVFP4) or 2 (MXFP4)
+  static constexpr int StepsPerAtom = SFVecSize / 16;
+  static constexpr int SfAtoms = KSteps / StepsPerAtom;
+  static constexpr int SFABytes = SfAtoms * 512;           // 2 KB NVFP4 (own 128 rows)
+  static constexpr int SFBBytes = 2 * SfAtoms * 512;       // 4 KB NVFP4 (all 256 rows)
   static constexpr int StageBytes = ABytes + BBytes + SFABytes + SFBBytes;
 
   static constexpr int NumWarps = 10;
@@ -61,7 +67,7 @@ struct Nvfp4Gemm2SmTraitsT {
   static constexpr uint32_t TmemCols = 512;
   static constexpr uint32_t AccCol = 0;
   static constexpr uint32_t SfCol = 256;
-  static constexpr uint32_t SfStride = 12 * KSteps;
+  static constexpr uint32_t SfStride = 12 * SfAtoms;
 
   // epilogue staging: one 32-row x 64-column BF16 box (4 KB, 128B-swizzled) per epilogue warp
   static constexpr int StoreBoxBytes = 32 * 64 * 2;
@@ -198,7 +204,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
           tma_load_2d_pair(sA + stage * KT::ABytes, &p.tmap_a, lb, kt * KT::RowBytes, a_row, pol);
           tma_load_2d_pair(sB + stage * KT::BBytes, &p.tmap_b, lb, kt * KT::RowBytes, b_row, pol);
           // one request per operand: SFA as one 2 KB row, SFB as the pair's two 2 KB rows
-          const int sf_y = p.sf_tail ? KT::KSteps * kt : kt;
+          const int sf_y = p.sf_tail ? KT::SfAtoms * kt : kt;
           tma_load_3d_pair(sSFA + stage * KT::SFABytes, &p.tmap_sfa, lb, 0, sf_y, sfa_blk, pol);
           tma_load_3d_pair(sSFB + stage * KT::SFBBytes, &p.tmap_sfb, lb, 0, sf_y, sfb_blk, pol);
           ++issued;
@@ -222,7 +228,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
     // Per k-tile: probe the next stage's barrier, copy this stage's scale factors to TMEM,
     // four MMAs, commit, then consume the probe (falling back to a bounded wait).
     if (rank == 0) {
-      constexpr uint32_t idesc = idesc_nvf4(KT::TileM, KT::TileN);
+      constexpr uint32_t idesc = idesc_bs(KT::TileM, KT::TileN, KT::Fmt::ScaleType);
       const uint32_t acc_full_0 = mapa_shared(acc_full, 0);
       const uint32_t acc_full_1 = mapa_shared(acc_full, 1);
       int stage = 0;
@@ -236,10 +242,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
         const uint32_t sfb_s = sSFB + st * KT::SFBBytes;
         const uint32_t ta = tmem + KT::SfCol + KT::SfStride * b;
 #pragma unroll
-        for (int j = 0; j < KT::KSteps; ++j) {
+        for (int j = 0; j < KT::SfAtoms; ++j) {
           tc_cp_32x128b_warpx4_pair_w(ta + 4 * j, desc_sf_atom(sfa_s + 512 * j));
-          tc_cp_32x128b_warpx4_pair_w(ta + 4 * KT::KSteps + 8 * j, desc_sf_atom(sfb_s + 512 * j));
-          tc_cp_32x128b_warpx4_pair_w(ta + 4 * KT::KSteps + 8 * j + 4,
+          tc_cp_32x128b_warpx4_pair_w(ta + 4 * KT::SfAtoms + 8 * j, desc_sf_atom(sfb_s + 512 * j));
+          tc_cp_32x128b_warpx4_pair_w(ta + 4 * KT::SfAtoms + 8 * j + 4,
                                       desc_sf_atom(sfb_s + KT::SFBBytes / 2 + 512 * j));
         }
       };
@@ -266,8 +272,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
           const uint32_t ta = tmem + KT::SfCol + KT::SfStride * sfbuf;
 #pragma unroll
           for (int j = 0; j < KT::KSteps; ++j) {
-            tc_mma_nvf4_pair_w(tmem + KT::AccCol, adesc + 2 * j, bdesc + 2 * j, idesc, ta + 4 * j,
-                               ta + 4 * KT::KSteps + 8 * j, (kt | j) != 0 ? 1u : 0u);
+            const int at = j / KT::StepsPerAtom;
+            const uint32_t sid = 2u * uint32_t(j % KT::StepsPerAtom);   // byte in the entry
+            tc_mma_nvf4_pair_w<KT::SFVecSize>(
+                tmem + KT::AccCol, adesc + 2 * j, bdesc + 2 * j, idesc_with_sf_id(idesc, sid),
+                sf_tmem_addr(ta + 4 * at, sid), sf_tmem_addr(ta + 4 * KT::SfAtoms + 8 * at, sid),
+                (kt | j) != 0 ? 1u : 0u);
           }
           tc_commit_pair_w(mapa_shared(empty_bar(stage), 0));
           tc_commit_pair_w(mapa_shared(empty_bar(stage), 1));
@@ -382,11 +392,11 @@ inline cudaError_t launch_2sm(int M, int N, int K, const void* A, const void* SF
   if (e != cudaSuccess) return e;
   // K % 256 != 0: 4 rows of 512 B per block, so that the K tail reads zeros (slower per k-tile)
   p.sf_tail = K % KT::TileK != 0;
-  e = p.sf_tail ? make_sf_tmap_atoms(&p.tmap_sfa, SFA, M, K, 1)
-                : make_sf_tmap_ktile(&p.tmap_sfa, SFA, M, K, 1, 1);
+  e = p.sf_tail ? make_sf_tmap_atoms(&p.tmap_sfa, SFA, M, K, 1, KT::SfAtoms, KT::SFVecSize)
+                : make_sf_tmap_ktile(&p.tmap_sfa, SFA, M, K, 1, 1, KT::SfAtoms, KT::SFVecSize);
   if (e != cudaSuccess) return e;
-  e = p.sf_tail ? make_sf_tmap_atoms(&p.tmap_sfb, SFB, N, K, 2)
-                : make_sf_tmap_ktile(&p.tmap_sfb, SFB, N, K, 2, 1);
+  e = p.sf_tail ? make_sf_tmap_atoms(&p.tmap_sfb, SFB, N, K, 2, KT::SfAtoms, KT::SFVecSize)
+                : make_sf_tmap_ktile(&p.tmap_sfb, SFB, N, K, 2, 1, KT::SfAtoms, KT::SFVecSize);
   if (e != cudaSuccess) return e;
   e = make_d_tmap(&p.tmap_d, D, M, N);
   if (e != cudaSuccess) return e;
@@ -399,7 +409,7 @@ inline cudaError_t launch_2sm(int M, int N, int K, const void* A, const void* SF
   p.tiles_n = (N + KT::TileN - 1) / KT::TileN;
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.k_tiles = (K + KT::TileK - 1) / KT::TileK;
-  p.sf_k_atoms = static_cast<int>(sf_k_atoms(K));
+  p.sf_k_atoms = static_cast<int>(sf_k_atoms_vs(K, KT::SFVecSize));
   // Persistent grid = the number of 2-CTA clusters that can be resident at once.  GPCs with
   // an odd number of usable SMs leave an SM idle, so this is below num_sms / 2; launching
   // num_sms / 2 clusters would run the excess as a second wave.

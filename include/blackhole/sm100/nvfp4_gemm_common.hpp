@@ -170,15 +170,17 @@ inline cudaError_t make_sf_tmap_uncached(CUtensorMap* m, const void* base, int64
 // on B200: every scale-factor request in flight slows the two-SM schedule's tensor pipe, far
 // beyond its bytes, so they are made few and long.)
 inline cudaError_t make_sf_tmap_ktile_uncached(CUtensorMap* m, const void* base, int64_t mn,
-                                               int64_t k, uint32_t blocks, uint32_t ktiles) {
+                                               int64_t k, uint32_t blocks, uint32_t ktiles,
+                                               int atoms_per_ktile, int vs) {
   EncodeTiledFn enc = encode_tiled_fn();
   if (!enc) return cudaErrorNotSupported;
-  const int64_t k_atoms = sf_k_atoms(k);
-  if (k_atoms % 4 != 0) return cudaErrorInvalidValue;
-  cuuint64_t dims[3] = {256u, static_cast<cuuint64_t>(k_atoms / 4),
+  const int64_t k_atoms = sf_k_atoms_vs(k, vs);
+  if (k_atoms % atoms_per_ktile != 0) return cudaErrorInvalidValue;
+  const uint32_t row_words = 64u * uint32_t(atoms_per_ktile);   // 8-byte elements per row
+  cuuint64_t dims[3] = {row_words, static_cast<cuuint64_t>(k_atoms / atoms_per_ktile),
                         static_cast<cuuint64_t>((mn + 127) / 128)};
-  cuuint64_t strides[2] = {2048u, static_cast<cuuint64_t>(k_atoms * 512)};
-  cuuint32_t box[3] = {256u, ktiles, blocks};
+  cuuint64_t strides[2] = {row_words * 8u, static_cast<cuuint64_t>(k_atoms * 512)};
+  cuuint32_t box[3] = {row_words, ktiles, blocks};
   cuuint32_t estr[3] = {1u, 1u, 1u};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<void*>(base), dims, strides,
                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -191,14 +193,15 @@ inline cudaError_t make_sf_tmap_ktile_uncached(CUtensorMap* m, const void* base,
 // and atoms past the last one of a block (the K tail) read zeros instead of running into the
 // next block or past the end of the buffer.
 inline cudaError_t make_sf_tmap_atoms_uncached(CUtensorMap* m, const void* base, int64_t mn,
-                                               int64_t k, uint32_t blocks) {
+                                               int64_t k, uint32_t blocks, uint32_t atoms,
+                                               int vs) {
   EncodeTiledFn enc = encode_tiled_fn();
   if (!enc) return cudaErrorNotSupported;
-  const int64_t k_atoms = sf_k_atoms(k);
+  const int64_t k_atoms = sf_k_atoms_vs(k, vs);
   cuuint64_t dims[3] = {64u, static_cast<cuuint64_t>(k_atoms),
                         static_cast<cuuint64_t>((mn + 127) / 128)};
   cuuint64_t strides[2] = {512u, static_cast<cuuint64_t>(k_atoms * 512)};
-  cuuint32_t box[3] = {64u, 4u, blocks};
+  cuuint32_t box[3] = {64u, atoms, blocks};
   cuuint32_t estr[3] = {1u, 1u, 1u};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<void*>(base), dims, strides,
                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -239,15 +242,18 @@ inline cudaError_t make_sf_tmap(CUtensorMap* m, const void* base, int64_t mn, in
   });
 }
 inline cudaError_t make_sf_tmap_ktile(CUtensorMap* m, const void* base, int64_t mn, int64_t k,
-                                      uint32_t blocks, uint32_t ktiles) {
-  return cached_tmap({3, base, mn, k, blocks, ktiles}, m, [&](CUtensorMap* o) {
-    return make_sf_tmap_ktile_uncached(o, base, mn, k, blocks, ktiles);
-  });
+                                      uint32_t blocks, uint32_t ktiles, int atoms_per_ktile = 4,
+                                      int vs = 16) {
+  return cached_tmap({3 + 16 * vs + 256 * atoms_per_ktile, base, mn, k, blocks, ktiles}, m,
+                     [&](CUtensorMap* o) {
+                       return make_sf_tmap_ktile_uncached(o, base, mn, k, blocks, ktiles,
+                                                          atoms_per_ktile, vs);
+                     });
 }
 inline cudaError_t make_sf_tmap_atoms(CUtensorMap* m, const void* base, int64_t mn, int64_t k,
-                                      uint32_t blocks) {
-  return cached_tmap({4, base, mn, k, blocks, 0}, m, [&](CUtensorMap* o) {
-    return make_sf_tmap_atoms_uncached(o, base, mn, k, blocks);
+                                      uint32_t blocks, uint32_t atoms = 4, int vs = 16) {
+  return cached_tmap({4 + 16 * vs, base, mn, k, blocks, atoms}, m, [&](CUtensorMap* o) {
+    return make_sf_tmap_atoms_uncached(o, base, mn, k, blocks, atoms, vs);
   });
 }
 inline cudaError_t make_d_tmap(CUtensorMap* m, void* base, int64_t rows, int64_t cols,

@@ -30,12 +30,15 @@
 
 #include <cstdint>
 
+#include <blackhole/sm100/block_scale_format.hpp>
 #include <blackhole/sm100/nvfp4_gemm_common.hpp>
 
 namespace blackhole::sm100 {
 
-template <int MPAD_>
+template <int MPAD_, class Fmt_ = Nvfp4Format>
 struct Nvfp4SkinnyTraits {
+  using Fmt = Fmt_;
+  static constexpr int SFVecSize = Fmt::SfVec;
   static constexpr int MPAD = MPAD_;            // UMMA N
   static constexpr int TileW = 128;             // rows of B per unit (UMMA M)
   static constexpr int TileK = 256;
@@ -43,7 +46,10 @@ struct Nvfp4SkinnyTraits {
   static constexpr int RowBytes = 128;
   static constexpr int WBytes = TileW * RowBytes;           // 16 KB
   static constexpr int XBytes = MPAD * RowBytes;            // 2..16 KB
-  static constexpr int SFBytes = KSteps * 512;              // 2 KB per operand
+  // scale-factor atoms per 128 rows and k-tile: 4 (NVFP4) or 2 (MXFP4)
+  static constexpr int StepsPerAtom = SFVecSize / 16;
+  static constexpr int SfAtoms = KSteps / StepsPerAtom;
+  static constexpr int SFBytes = SfAtoms * 512;             // 2 KB per operand (NVFP4)
   static constexpr int StageBytes = WBytes + XBytes + 2 * SFBytes;
   static constexpr int Stages = (MPAD <= 32) ? 9 : (MPAD == 64 ? 8 : 6);
   // k-tiles of B prefetched into L2 before the dependency wait (beyond the smem stages)
@@ -65,8 +71,8 @@ struct Nvfp4SkinnyTraits {
 
   static constexpr uint32_t TmemCols = 512;
   static constexpr uint32_t AccStride = 128;                // two accumulators: [0,128), [128,256)
-  static constexpr uint32_t SfwCol = 256;                   // 4 columns per k-step
-  static constexpr uint32_t SfxCol = 256 + 4 * KSteps;      // 4 columns per k-step
+  static constexpr uint32_t SfwCol = 256;                   // 4 columns per atom
+  static constexpr uint32_t SfxCol = 256 + 4 * SfAtoms;     // 4 columns per atom
 
   static constexpr int BarrierBytes = 8 * (2 * Stages + 5) + 16;
   static constexpr int SmemBytes = Stages * StageBytes + BarrierBytes + 1024;
@@ -273,9 +279,9 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
         }
         const int kt = kta++;
         tma_prefetch_l2_2d(&p.tmap_w, kt * KT::RowBytes, sa.rb * KT::TileW);
-        // only the atoms that exist (the last k-tile of a K tail has fewer than 4)
-        const int atoms = min(KT::KSteps, p.sf_k_atoms - KT::KSteps * kt);
-        bulk_prefetch_l2(p.sfw + int64_t(sa.rb) * p.sf_k_atoms * 512 + int64_t(kt) * KT::KSteps * 512,
+        // only the atoms that exist (the last k-tile of a K tail has fewer)
+        const int atoms = min(KT::SfAtoms, p.sf_k_atoms - KT::SfAtoms * kt);
+        bulk_prefetch_l2(p.sfw + int64_t(sa.rb) * p.sf_k_atoms * 512 + int64_t(kt) * KT::SfAtoms * 512,
                          uint32_t(atoms) * 512u);
       };
       for (int i = 0; i < p.l2_pf; ++i) prefetch_next();
@@ -294,17 +300,17 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
             break;
           }
           const uint32_t fb = full_bar(stage);
-          const int64_t k_off = int64_t(kt) * KT::KSteps * 512;
+          const int64_t k_off = int64_t(kt) * KT::SfAtoms * 512;
           mbar_arrive_expect_tx(fb, KT::StageBytes);
           // A (small, L2-resident) ahead of B in the copy engine's queue
           tma_load_2d(st_x(stage), &p.tmap_x, fb, kt * KT::RowBytes, 0, pol_x);
           if (p.sf_tail)  // atoms past K read zeros
-            tma_load_3d(st_sfx(stage), &p.tmap_sfx, fb, 0, KT::KSteps * kt, 0, pol_x);
+            tma_load_3d(st_sfx(stage), &p.tmap_sfx, fb, 0, KT::SfAtoms * kt, 0, pol_x);
           else
             bulk_load(st_sfx(stage), p.sfx + k_off, KT::SFBytes, fb, pol_x);
           tma_load_2d(st_w(stage), &p.tmap_w, fb, kt * KT::RowBytes, sg.rb * KT::TileW, pol_w);
           if (p.sf_tail)
-            tma_load_3d(st_sfw(stage), &p.tmap_sfw, fb, 0, KT::KSteps * kt, sg.rb, pol_w);
+            tma_load_3d(st_sfw(stage), &p.tmap_sfw, fb, 0, KT::SfAtoms * kt, sg.rb, pol_w);
           else
             bulk_load(st_sfw(stage), sfw_rb + k_off, KT::SFBytes, fb, pol_w);
           ++issued;
@@ -325,7 +331,7 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
     }
   } else if (warp == KT::MmaWarp) {
     // ------------------------------ MMA issuer --------------------------------------
-    constexpr uint32_t idesc = idesc_nvf4(128, MPAD);
+    constexpr uint32_t idesc = idesc_bs(128, MPAD, KT::Fmt::ScaleType);
     int stage = 0;
     uint32_t phase = 0;
     int acc = 0;
@@ -352,7 +358,7 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
         const uint32_t ready = more ? mbar_probe(full_bar(nstage), nphase) : 1u;
         {
 #pragma unroll
-          for (int j = 0; j < KT::KSteps; ++j) {
+          for (int j = 0; j < KT::SfAtoms; ++j) {
             tc_cp_32x128b_warpx4_w(tmem + KT::SfwCol + 4 * j, desc_sf_atom(st_sfw(stage) + 512 * j));
             tc_cp_32x128b_warpx4_w(tmem + KT::SfxCol + 4 * j, desc_sf_atom(st_sfx(stage) + 512 * j));
           }
@@ -360,8 +366,12 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
           const uint64_t xdesc = desc_kmajor_sw128(st_x(stage));
 #pragma unroll
           for (int j = 0; j < KT::KSteps; ++j) {
-            tc_mma_nvf4_w(d_tmem, wdesc + 2 * j, xdesc + 2 * j, idesc, tmem + KT::SfwCol + 4 * j,
-                          tmem + KT::SfxCol + 4 * j, (kt != sg.kt0 || j != 0) ? 1u : 0u);
+            const int at = j / KT::StepsPerAtom;
+            const uint32_t sid = 2u * uint32_t(j % KT::StepsPerAtom);   // byte in the entry
+            tc_mma_nvf4_w<KT::SFVecSize>(
+                d_tmem, wdesc + 2 * j, xdesc + 2 * j, idesc_with_sf_id(idesc, sid),
+                sf_tmem_addr(tmem + KT::SfwCol + 4 * at, sid),
+                sf_tmem_addr(tmem + KT::SfxCol + 4 * at, sid), (kt != sg.kt0 || j != 0) ? 1u : 0u);
           }
           tc_commit_w(empty_bar(stage));
           issued_any = true;
@@ -528,9 +538,9 @@ inline cudaError_t launch_skinny(int M, int N, int K, const void* A, const void*
   p.kt_per_rb = (K + KT::TileK - 1) / KT::TileK;
   p.sf_tail = K % KT::TileK != 0;
   if (p.sf_tail) {
-    e = make_sf_tmap_atoms(&p.tmap_sfw, SFB, N, K, 1);
+    e = make_sf_tmap_atoms(&p.tmap_sfw, SFB, N, K, 1, KT::SfAtoms, KT::SFVecSize);
     if (e != cudaSuccess) return e;
-    e = make_sf_tmap_atoms(&p.tmap_sfx, SFA, M, K, 1);
+    e = make_sf_tmap_atoms(&p.tmap_sfx, SFA, M, K, 1, KT::SfAtoms, KT::SFVecSize);
     if (e != cudaSuccess) return e;
   }
   p.units = int64_t((N + 127) / 128) * p.kt_per_rb;
@@ -554,7 +564,7 @@ inline cudaError_t launch_skinny(int M, int N, int K, const void* A, const void*
             p.units < (int64_t(1) << 62) / (128 * int64_t(grid) * grid))
                ? skew
                : 0;
-  p.sf_k_atoms = static_cast<int>(sf_k_atoms(K));
+  p.sf_k_atoms = static_cast<int>(sf_k_atoms_vs(K, KT::SFVecSize));
   p.l2_pf = prefetch ? l2_prefetch_ktiles : 0;
   e = launch_pdl(nvfp4_gemm_skinny_kernel<KT>, dim3(grid), dim3(KT::NumThreads), KT::SmemBytes,
                  stream, p);
@@ -572,11 +582,13 @@ inline cudaError_t launch_skinny(int M, int N, int K, const void* A, const void*
 // the stream, issues L2 prefetches of the first B / SFB tiles of its range while that kernel
 // is finishing; every load, store and workspace access still waits for its completion, so
 // the results are those of plain stream order either way.
-inline cudaError_t nvfp4_bf16_gemm_skinny(int M, int N, int K, void const* A, void const* SFA,
-                                          void const* B, void const* SFB, void* D, float alpha,
-                                          void* workspace, int64_t workspace_bytes,
-                                          cudaStream_t stream = nullptr, int grid_cap = 1 << 30,
-                                          bool prefetch = true) {
+template <class Fmt = Nvfp4Format>
+inline cudaError_t block_scaled_bf16_gemm_skinny(int M, int N, int K, void const* A,
+                                                 void const* SFA, void const* B, void const* SFB,
+                                                 void* D, float alpha, void* workspace,
+                                                 int64_t workspace_bytes,
+                                                 cudaStream_t stream = nullptr,
+                                                 int grid_cap = 1 << 30, bool prefetch = true) {
   cudaError_t e = nvfp4_check_args(M, N, K, A, SFA, B, SFB, D);
   if (e != cudaSuccess) return e;
   if (M > 128 || !workspace || (reinterpret_cast<uintptr_t>(workspace) & 15u))
@@ -586,18 +598,28 @@ inline cudaError_t nvfp4_bf16_gemm_skinny(int M, int N, int K, void const* A, vo
   if (st->init_err != cudaSuccess) return st->init_err;
   switch (nvfp4_skinny_mpad(M)) {
     case 16:
-      return detail::launch_skinny<Nvfp4SkinnyTraits<16>>(M, N, K, A, SFA, B, SFB, D, alpha, workspace,
-                                                           workspace_bytes, grid_cap, prefetch, st, stream);
+      return detail::launch_skinny<Nvfp4SkinnyTraits<16, Fmt>>(
+          M, N, K, A, SFA, B, SFB, D, alpha, workspace, workspace_bytes, grid_cap, prefetch, st, stream);
     case 32:
-      return detail::launch_skinny<Nvfp4SkinnyTraits<32>>(M, N, K, A, SFA, B, SFB, D, alpha, workspace,
-                                                           workspace_bytes, grid_cap, prefetch, st, stream);
+      return detail::launch_skinny<Nvfp4SkinnyTraits<32, Fmt>>(
+          M, N, K, A, SFA, B, SFB, D, alpha, workspace, workspace_bytes, grid_cap, prefetch, st, stream);
     case 64:
-      return detail::launch_skinny<Nvfp4SkinnyTraits<64>>(M, N, K, A, SFA, B, SFB, D, alpha, workspace,
-                                                           workspace_bytes, grid_cap, prefetch, st, stream);
+      return detail::launch_skinny<Nvfp4SkinnyTraits<64, Fmt>>(
+          M, N, K, A, SFA, B, SFB, D, alpha, workspace, workspace_bytes, grid_cap, prefetch, st, stream);
     default:
-      return detail::launch_skinny<Nvfp4SkinnyTraits<128>>(M, N, K, A, SFA, B, SFB, D, alpha, workspace,
-                                                            workspace_bytes, grid_cap, prefetch, st, stream);
+      return detail::launch_skinny<Nvfp4SkinnyTraits<128, Fmt>>(
+          M, N, K, A, SFA, B, SFB, D, alpha, workspace, workspace_bytes, grid_cap, prefetch, st, stream);
   }
+}
+
+// The NVFP4 operator's skinny schedule (the reference's format).
+inline cudaError_t nvfp4_bf16_gemm_skinny(int M, int N, int K, void const* A, void const* SFA,
+                                          void const* B, void const* SFB, void* D, float alpha,
+                                          void* workspace, int64_t workspace_bytes,
+                                          cudaStream_t stream = nullptr, int grid_cap = 1 << 30,
+                                          bool prefetch = true) {
+  return block_scaled_bf16_gemm_skinny<Nvfp4Format>(M, N, K, A, SFA, B, SFB, D, alpha, workspace,
+                                                    workspace_bytes, stream, grid_cap, prefetch);
 }
 
 #endif  // __CUDACC__

@@ -165,6 +165,52 @@ __global__ void __launch_bounds__(256) quantize_kernel(const T* __restrict__ x, 
   sf[blackhole::sf_offset(r, kg, K)] = static_cast<uint8_t>(s_code);
 }
 
+// MXFP4 (OCP MX v1.0): one thread per (row, 32-element group) over the padded extent.
+// Shared exponent e = floor(log2(amax_b)) - 2, read from amax_b's exponent bits (zero and
+// subnormal amax -> -127), clamped to [-127, 127]; scale code e + 127; element codes
+// e2m1(x * 2^-e) with the power of two built exactly.  Padding entries get code 0.
+template <class T>
+__global__ void __launch_bounds__(256) mx_quantize_kernel(const T* __restrict__ x, int rows, int K,
+                                                          uint8_t* __restrict__ packed,
+                                                          uint8_t* __restrict__ sf) {
+  const int groups = K / 32;
+  const int groups_pad = (groups + 3) / 4 * 4;
+  const int64_t rows_pad = (int64_t(rows) + 127) / 128 * 128;
+  const int64_t idx = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;
+  if (idx >= rows_pad * groups_pad) return;
+  const int64_t r = idx / groups_pad;
+  const int64_t kg = idx - r * groups_pad;
+  uint32_t code = 0;
+  if (r < rows && kg < groups) {
+    float v[32];
+    float lo16[16], hi16[16];
+    load16(x + r * K + kg * 32, lo16);
+    load16(x + r * K + kg * 32 + 16, hi16);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      v[i] = lo16[i];
+      v[16 + i] = hi16[i];
+    }
+    float amax_b = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) amax_b = fmaxf(amax_b, fabsf(v[i]));
+    const int ebits = static_cast<int>((__float_as_uint(amax_b) >> 23) & 0xFFu);
+    int e = ebits == 0 ? -127 : ebits - 129;
+    e = max(-127, min(127, e));
+    code = static_cast<uint32_t>(e + 127);
+    const float inv = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);
+    uint32_t w[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      w[q] = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w[q] |= e2m1_rne(v[8 * q + i] * inv) << (4 * i);
+    }
+    *reinterpret_cast<uint4*>(packed + (r * K + kg * 32) / 2) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  sf[blackhole::sf_offset_vs(r, kg, K, 32)] = static_cast<uint8_t>(code);
+}
+
 }  // namespace quant_detail
 
 // X: rows x K (FP32 if x_is_bf16 == 0, else BF16), K % 16 == 0, 16-byte aligned.
@@ -198,6 +244,29 @@ inline cudaError_t nvfp4_quantize(const void* X, int x_is_bf16, int rows, int K,
     quant_detail::quantize_kernel<<<static_cast<int>(qgrid), 256, 0, stream>>>(
         xp, rows, K, static_cast<uint8_t*>(packed), static_cast<uint8_t*>(sf), scales);
   }
+  return cudaGetLastError();
+}
+
+// MXFP4 quantiser: X rows x K (FP32 if x_is_bf16 == 0, else BF16), K % 32 == 0, 16-byte
+// aligned.  packed: rows*K/2 bytes (16-byte aligned).  sf: sf_storage_bytes_vs(rows, K, 32)
+// bytes, every padding byte written 0.  No global scale: alpha of an MXFP4 GEMM is 1 (or the
+// caller's own).
+inline cudaError_t mxfp4_quantize(const void* X, int x_is_bf16, int rows, int K, void* packed,
+                                  void* sf, cudaStream_t stream = nullptr) {
+  if (rows < 1 || K < 32 || K % 32 != 0 || !X || !packed || !sf) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(X) & 15u) || (reinterpret_cast<uintptr_t>(packed) & 15u))
+    return cudaErrorInvalidValue;
+  const int64_t work = (int64_t(rows) + 127) / 128 * 128 * ((K / 32 + 3) / 4 * 4);
+  const int64_t grid = (work + 255) / 256;
+  if (grid > 0x7FFFFFFF) return cudaErrorInvalidValue;
+  if (x_is_bf16)
+    quant_detail::mx_quantize_kernel<<<static_cast<int>(grid), 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(X), rows, K, static_cast<uint8_t*>(packed),
+        static_cast<uint8_t*>(sf));
+  else
+    quant_detail::mx_quantize_kernel<<<static_cast<int>(grid), 256, 0, stream>>>(
+        static_cast<const float*>(X), rows, K, static_cast<uint8_t*>(packed),
+        static_cast<uint8_t*>(sf));
   return cudaGetLastError();
 }
 

@@ -260,17 +260,31 @@ __device__ __forceinline__ void tc_cp_32x128b_warpx4_w(uint32_t taddr, uint64_t 
       "l"(sdesc)
       : "memory");
 }
+// SfVec = 16: scale blocks of 16 elements (NVFP4); 32: blocks of 32 (MXFP4).
+template <int SfVec = 16>
 __device__ __forceinline__ void tc_mma_nvf4_w(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                               uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
                                               uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p, P;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "elect.sync _|P, 0xffffffff;\n\t"
-      "@P tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t"
-      "}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
-      : "memory");
+  static_assert(SfVec == 16 || SfVec == 32, "scale block");
+  if constexpr (SfVec == 16) {
+    asm volatile(
+        "{\n\t.reg .pred p, P;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "elect.sync _|P, 0xffffffff;\n\t"
+        "@P tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t"
+        "}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p, P;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "elect.sync _|P, 0xffffffff;\n\t"
+        "@P tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n\t"
+        "}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+        : "memory");
+  }
 }
 __device__ __forceinline__ void tc_commit_w(uint32_t bar) {
   asm volatile(
@@ -285,17 +299,30 @@ __device__ __forceinline__ void tc_cp_32x128b_warpx4_pair_w(uint32_t taddr, uint
       "l"(sdesc)
       : "memory");
 }
+template <int SfVec = 16>
 __device__ __forceinline__ void tc_mma_nvf4_pair_w(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                                    uint32_t idesc, uint32_t sfa_tmem,
                                                    uint32_t sfb_tmem, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p, P;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "elect.sync _|P, 0xffffffff;\n\t"
-      "@P tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t"
-      "}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
-      : "memory");
+  static_assert(SfVec == 16 || SfVec == 32, "scale block");
+  if constexpr (SfVec == 16) {
+    asm volatile(
+        "{\n\t.reg .pred p, P;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "elect.sync _|P, 0xffffffff;\n\t"
+        "@P tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t"
+        "}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p, P;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "elect.sync _|P, 0xffffffff;\n\t"
+        "@P tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n\t"
+        "}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+        : "memory");
+  }
 }
 __device__ __forceinline__ void tc_commit_pair_w(uint32_t cluster_bar) {
   asm volatile(
@@ -455,6 +482,21 @@ __device__ __forceinline__ uint64_t desc_sf_atom(uint32_t saddr) {
 __host__ __device__ constexpr uint32_t idesc_nvf4(int m, int n) {
   return (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
          (static_cast<uint32_t>(m >> 4) << 24);
+}
+// With the scale-factor format (bit 23: 0 = UE4M3, 1 = UE8M0).
+__host__ __device__ constexpr uint32_t idesc_bs(int m, int n, uint32_t scale_type) {
+  return idesc_nvf4(m, n) | (scale_type << 23);
+}
+// Scale-factor byte ID of both operands (bits 29-30 for A, 4-5 for B): which byte of each
+// 32-bit scale-factor column an MMA starts at.  With 32-element blocks an atom (4 bytes per
+// row) serves two 64-element MMAs: the first reads bytes 0-1 (ID 0), the second 2-3 (ID 2).
+__host__ __device__ constexpr uint32_t idesc_with_sf_id(uint32_t idesc, uint32_t id) {
+  return idesc | (id << 29) | (id << 4);
+}
+// The same byte ID also rides in bits 30-31 of the scale-factor TMEM address operand (the
+// lane field of these addresses is 0; CUTLASS's UMMA atoms pass it the same way).
+__host__ __device__ constexpr uint32_t sf_tmem_addr(uint32_t taddr, uint32_t id) {
+  return taddr | (id << 30);
 }
 
 __device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, uint32_t c,

@@ -15,7 +15,7 @@
 extern "C" {
 #endif
 
-#define BLACKHOLE_SM100_ABI_VERSION 1
+#define BLACKHOLE_SM100_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define BLACKHOLE_SM100_API __attribute__((visibility("default")))
@@ -114,6 +114,34 @@ BLACKHOLE_SM100_API int blackhole_sm100_nvfp4_bf16_gemm_noalloc(int M, int N, in
  * Asynchronous on `stream`; read the status with blackhole_sm100_device_status. */
 BLACKHOLE_SM100_API int blackhole_sm100_selftest_bounded_wait(uint64_t limit_ns, uint64_t* result,
                                                               cudaStream_t stream);
+
+/* MXFP4 x MXFP4 -> BF16 (OCP Microscaling v1.0: E2M1 elements, one UE8M0 scale per 32
+ * elements along K, in the same 128x4 blocked layout with 32-element groups).  No
+ * counterpart in the reference, which serves NVFP4 only: the sibling format behind the same
+ * operator shape.  Arguments, shapes, ordering and errors as blackhole_sm100_nvfp4_bf16_gemm;
+ * SFA / SFB span blackhole_sm100_mxfp4_sf_storage_bytes(M|N, K) bytes; alpha = 1 is plain
+ * MXFP4. */
+BLACKHOLE_SM100_API int blackhole_sm100_mxfp4_bf16_gemm(int M, int N, int K, const void* A,
+                                                        const void* SFA, const void* B,
+                                                        const void* SFB, void* D, float alpha,
+                                                        cudaStream_t stream);
+/* With an explicit schedule and workspace, as blackhole_sm100_nvfp4_bf16_gemm_ex. */
+BLACKHOLE_SM100_API int blackhole_sm100_mxfp4_bf16_gemm_ex(int M, int N, int K, const void* A,
+                                                           const void* SFA, const void* B,
+                                                           const void* SFB, void* D, float alpha,
+                                                           int schedule, void* workspace,
+                                                           int64_t workspace_bytes,
+                                                           cudaStream_t stream);
+/* Bytes of an (mn, k) MXFP4 scale-factor tensor (rows padded to 128, 32-element groups
+ * padded to a multiple of 4); negative on error. */
+BLACKHOLE_SM100_API int64_t blackhole_sm100_mxfp4_sf_storage_bytes(int64_t mn, int64_t k);
+/* MXFP4 quantiser: X (rows x K, FP32 when x_is_bf16 == 0, else BF16, K % 32 == 0, 16-byte
+ * aligned) -> packed E2M1 (rows*K/2 bytes, 16-byte aligned) and UE8M0 scales (padding written
+ * 0).  Per 32-block: e = floor(log2(amax_b)) - 2 clamped to [-127, 127], scale 2^e,
+ * q = E2M1(x * 2^-e) round-to-nearest-even, saturating at 6. */
+BLACKHOLE_SM100_API int blackhole_sm100_mxfp4_quantize(const void* X, int x_is_bf16, int rows,
+                                                       int K, void* packed, void* sf,
+                                                       cudaStream_t stream);
 
 /* ABI version of the loaded library (BLACKHOLE_SM100_ABI_VERSION). */
 BLACKHOLE_SM100_API int blackhole_sm100_abi_version(void);

@@ -34,7 +34,8 @@ def test_library_exports_every_declared_symbol():
     L = bh.load()
     for s in syms:
         assert hasattr(L, s)
-    assert L.blackhole_sm100_abi_version() == 1
+    assert L.blackhole_sm100_abi_version() == 2
+    assert "blackhole_sm100_mxfp4_bf16_gemm_ex" in syms and "blackhole_sm100_mxfp4_quantize" in syms
 
 
 @pytest.mark.parametrize("mn,k", [(1, 256), (16, 8192), (200, 768), (28672, 8192), (8192, 8192)])
@@ -45,6 +46,20 @@ def test_sf_layout_matches_oracle(mn, k):
             continue
         for kg in (0, 1, 3, 4, k // 16 - 1):
             assert bh.sf_offset(m, kg, k) == O.sf_offset(m, kg, k)
+
+
+@pytest.mark.parametrize("mn,k", [(1, 128), (16, 8192), (200, 768), (130, 320), (8192, 8192)])
+def test_mx_sf_layout_matches_oracle(mn, k):
+    assert bh.mxfp4_sf_storage_bytes(mn, k) == O.sf_storage_bytes_vs(mn, k, 32)
+
+
+@pytest.mark.parametrize("M,N,K", [(0, 128, 256), (128, 100, 256), (128, 128, 16), (128, 128, 48),
+                                   (128, 4, 256)])
+def test_mx_bad_shapes_rejected_before_launch(M, N, K):
+    for sched in ("auto", "1sm", "2sm", "skinny"):
+        with pytest.raises(bh.BlackholeError) as ei:
+            bh.mxfp4_bf16_gemm(M, N, K, 4096, 4096, 4096, 4096, 4096, 1.0, stream=0, schedule=sched)
+        assert ei.value.code == 1
 
 
 @pytest.mark.parametrize("M,N,K", [(0, 128, 256), (128, 0, 256), (128, 100, 256), (128, 128, 0),
