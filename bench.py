@@ -205,7 +205,7 @@ def gemm_bytes(M, N, K):
     return M * K // 2 + N * K // 2 + M * K // 16 + N * K // 16 + 2 * M * N
 
 
-def time_gemm(M, N, K, sets, D, steps, warmup, world, schedule="auto"):
+def time_gemm(M, N, K, sets, D, steps, warmup, world, schedule="auto", fmt="nvfp4"):
     """Back-to-back launches cycling through the input sets; returns total ms of `steps`
     launches from CUDA events on the launching stream (one event pair around all of them)."""
     import torch
@@ -214,7 +214,9 @@ def time_gemm(M, N, K, sets, D, steps, warmup, world, schedule="auto"):
     stream = torch.cuda.current_stream()
 
     def launch(A, SFA, B, SFB, alpha):
-        if schedule == "auto":
+        if fmt == "mxfp4":
+            bh.mxfp4_bf16_gemm(M, N, K, A, SFA, B, SFB, D, alpha, schedule=schedule)
+        elif schedule == "auto":
             bh.nvfp4_bf16_gemm(M, N, K, A, SFA, B, SFB, D, alpha)
         else:
             bh.nvfp4_bf16_gemm_ex(M, N, K, A, SFA, B, SFB, D, alpha, schedule=schedule)
@@ -428,6 +430,52 @@ def run_decode(args, dev, rank, world, hbm_peak, peak_src, Ms=(16, 1, 64, 128)):
     return out
 
 
+def run_mxfp4(args, dev, rank, world, fp4_peak, hbm_peak):
+    """The MXFP4 sibling (UE8M0 scale per 32) on configs[1]'s and configs[2]'s M=16 shapes,
+    same sources (N(0,1); decode weights N(0, 0.02^2)), quantised on the device."""
+    import torch
+    import blackhole_b200 as bh
+
+    def mx_operand(rows, K, seed, std):
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        x = torch.randn((rows, K), generator=g, device=dev, dtype=torch.float32)
+        if std != 1.0:
+            x.mul_(std)
+        packed, sf = bh.quantize_tensor_mxfp4(x)
+        torch.cuda.synchronize()
+        return packed, sf
+
+    out = {}
+    M = N = K = 8192
+    sets = [mx_operand(M, K, 1 + 7 * i, 1.0) + mx_operand(N, K, 1000 + rank + 7 * i, 1.0) + (1.0,)
+            for i in range(4)]
+    D = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    steps = max(10, min(args.steps, 400))
+    tot = time_gemm(M, N, K, sets, D, steps, max(3, args.warmup), world, fmt="mxfp4")
+    ms = max_over_ranks(tot / steps, world)
+    tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+    out["gemm_8192"] = {"value": tf * world, "unit": "TFLOP/s", "ms_per_step": ms, "steps": steps,
+                        "roofline_frac": tf / fp4_peak,
+                        "l2": "4 rotating input sets (~290 MB > 126 MB L2), back to back"}
+    del sets, D
+    Md, Nd, Kd = 16, 28672, 8192
+    dsets = [mx_operand(Md, Kd, 2 + 7 * i, 1.0) + mx_operand(Nd, Kd, 2000 + rank + 7 * i, 0.02) + (1.0,)
+             for i in range(3)]
+    Dd = torch.empty((Md, Nd), dtype=torch.bfloat16, device=dev)
+    dsteps = max(30, min(args.steps, 2000))
+    tot = time_gemm(Md, Nd, Kd, dsets, Dd, dsteps, max(3, args.warmup), world, fmt="mxfp4")
+    dms = max_over_ranks(tot / dsteps, world)
+    nbytes = Md * Kd // 2 + Nd * Kd // 2 + (Md + Nd) * Kd // 32 + 2 * Md * Nd
+    gbs = nbytes / (dms * 1e-3) / 1e9
+    out["decode_m16"] = {"value": gbs * world, "unit": "GB/s", "ms_per_step": dms, "steps": dsteps,
+                         "bytes_per_launch": nbytes, "roofline_frac": gbs / hbm_peak,
+                         "l2": "3 rotating weight sets (~380 MB > 126 MB L2), back to back"}
+    del dsets, Dd
+    out["steps"] = steps + dsteps
+    return out
+
+
 def run_prefill(args, dev, rank, world, fp4_peak):
     """M=16384 N=8192 K=28672, A from N(0,1) with 1% of entries x20, B from
     N(0, 0.02^2); 2 rotating input sets (~800 MB), back to back."""
@@ -486,6 +534,35 @@ def run_nsplit(args, dev, rank, world, fp4_peak):
                          "bytes_per_gpu_in": (world - 1) * M * sh.rows * 2,
                          "with_gather_tflops": flops / ((ms + gms) * 1e-3) / 1e12}
         del g
+        # the gather fused into the GEMM: each rank's epilogue stores its tiles into every
+        # rank's row-major M x N buffer (CUDA IPC mappings) while it computes the next tiles;
+        # a one-element NCCL all-reduce per step is the completion barrier
+        import blackhole_b200 as bh
+        from blackhole_b200.nsplit import GatheredOutput
+
+        go = GatheredOutput(M, N, rank, world)
+
+        def fused():
+            bh.nvfp4_bf16_gemm_gather(M, sh.rows, K, A, SFA, B, SFB, go.dst, sh.row0, N, alpha)
+            go.barrier()
+
+        for _ in range(2):
+            fused()
+        barrier(world)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(steps):
+            fused()
+        e.record()
+        barrier(world)
+        fms = max_over_ranks(s.elapsed_time(e) / steps, world)
+        out["fused_gather"] = {"ms_per_step": fms, "tflops": flops / (fms * 1e-3) / 1e12,
+                               "layout": "row-major M x N on every GPU",
+                               "nvlink_bytes_out_per_gpu": (world - 1) * M * sh.rows * 2,
+                               "speedup_vs_gemm_then_nccl": (ms + gms) / fms, "steps": steps}
+        out["steps"] += steps
+        go.close()
+        del go
     del A, SFA, B, SFB, D
     return out
 
@@ -580,6 +657,8 @@ def main():
         result["prefill"] = run_prefill(args, dev, rank, world, fp4_peak)
         result["nsplit"] = run_nsplit(args, dev, rank, world, fp4_peak)
         result["gpu_launches"] += result["prefill"]["steps"] + result["nsplit"]["steps"]
+        result["mxfp4"] = run_mxfp4(args, dev, rank, world, fp4_peak, hbm_peak)
+        result["gpu_launches"] += result["mxfp4"]["steps"]
 
     if world > 1 and args.gather:
         import torch.distributed as dist

@@ -18,7 +18,7 @@ __all__ = [
     "device_status", "BlackholeError", "nvfp4_quantize", "quantize_tensor",
     "nvfp4_bf16_gemm_ex", "workspace_bytes", "SCHEDULES", "nvfp4_bf16_gemm_noalloc",
     "selftest_bounded_wait", "mxfp4_bf16_gemm", "mxfp4_sf_storage_bytes", "mxfp4_quantize",
-    "quantize_tensor_mxfp4",
+    "quantize_tensor_mxfp4", "nvfp4_bf16_gemm_gather", "ipc_get_handle", "ipc_open", "ipc_close",
 ]
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -79,6 +79,15 @@ def load():
     L.blackhole_sm100_nvfp4_quantize.argtypes = [vp, i32, i32, i32, vp, vp, vp, vp]
     L.blackhole_sm100_selftest_bounded_wait.restype = i32
     L.blackhole_sm100_selftest_bounded_wait.argtypes = [ctypes.c_uint64, vp, vp]
+    L.blackhole_sm100_nvfp4_bf16_gemm_gather.restype = i32
+    L.blackhole_sm100_nvfp4_bf16_gemm_gather.argtypes = [i32, i32, i32, vp, vp, vp, vp, vp, i32, i64,
+                                                         i64, ctypes.c_float, vp]
+    L.blackhole_sm100_ipc_get_handle.restype = i32
+    L.blackhole_sm100_ipc_get_handle.argtypes = [vp, vp, ctypes.POINTER(ctypes.c_int64)]
+    L.blackhole_sm100_ipc_open.restype = i32
+    L.blackhole_sm100_ipc_open.argtypes = [vp, i64, ctypes.POINTER(ctypes.c_void_p)]
+    L.blackhole_sm100_ipc_close.restype = i32
+    L.blackhole_sm100_ipc_close.argtypes = [vp]
     L.blackhole_sm100_abi_version.restype = i32
     L.blackhole_sm100_abi_version.argtypes = []
     _lib = L
@@ -185,6 +194,51 @@ def quantize_tensor_mxfp4(X, stream=None):
     sf = torch.empty(mxfp4_sf_storage_bytes(rows, K), dtype=torch.uint8, device=X.device)
     mxfp4_quantize(X, rows, K, packed, sf, x_is_bf16=(X.dtype == torch.bfloat16), stream=stream)
     return packed, sf
+
+
+def nvfp4_bf16_gemm_gather(M: int, N: int, K: int, A, SFA, B, SFB, dst, col0: int, ldd: int,
+                           alpha: float = 1.0, stream=None) -> None:
+    """GEMM whose M x N result is written to columns [col0, col0 + N) of every buffer in
+    `dst` (row-major BF16, rows `ldd` elements apart) from inside the kernel.  dst[0] must be
+    this GPU's memory; the others may be other GPUs' buffers mapped with ipc_open.  The caller
+    synchronises the ranks afterwards (nothing in the call waits for other GPUs)."""
+    ptrs = (ctypes.c_void_p * max(1, len(dst)))(*[_ptr(d) for d in dst])
+    rc = load().blackhole_sm100_nvfp4_bf16_gemm_gather(
+        int(M), int(N), int(K), _ptr(A), _ptr(SFA), _ptr(B), _ptr(SFB),
+        ctypes.cast(ptrs, ctypes.c_void_p) if dst else None, len(dst), int(col0), int(ldd),
+        float(alpha), _stream(stream))
+    if rc != 0:
+        raise BlackholeError("blackhole_sm100_nvfp4_bf16_gemm_gather", rc)
+
+
+def ipc_get_handle(buf):
+    """(64-byte CUDA IPC handle of the allocation holding `buf`, byte offset of `buf` in it)."""
+    h = (ctypes.c_char * 64)()
+    off = ctypes.c_int64(0)
+    rc = load().blackhole_sm100_ipc_get_handle(_ptr(buf), ctypes.cast(h, ctypes.c_void_p),
+                                               ctypes.byref(off))
+    if rc != 0:
+        raise BlackholeError("blackhole_sm100_ipc_get_handle", rc)
+    return bytes(h.raw), int(off.value)
+
+
+def ipc_open(handle: bytes, offset: int) -> int:
+    """Maps another process's buffer (from ipc_get_handle) on the current device; returns the
+    device address of the same byte."""
+    if len(handle) != 64:
+        raise ValueError("an IPC handle is 64 bytes")
+    h = (ctypes.c_char * 64).from_buffer_copy(handle)
+    out = ctypes.c_void_p(0)
+    rc = load().blackhole_sm100_ipc_open(ctypes.cast(h, ctypes.c_void_p), int(offset), ctypes.byref(out))
+    if rc != 0:
+        raise BlackholeError("blackhole_sm100_ipc_open", rc)
+    return int(out.value)
+
+
+def ipc_close(ptr: int) -> None:
+    rc = load().blackhole_sm100_ipc_close(int(ptr))
+    if rc != 0:
+        raise BlackholeError("blackhole_sm100_ipc_close", rc)
 
 
 def nvfp4_bf16_gemm_noalloc(M: int, N: int, K: int, A, SFA, B, SFB, D, alpha: float = 1.0,

@@ -8,6 +8,8 @@
 #include <blackhole/sm100/nvfp4_quant.hpp>
 #include <blackhole/sm100/bounded_wait_selftest.hpp>
 
+#include <cstring>
+#include <map>
 #include <mutex>
 
 // ---------------------------------------------------------------------------------------
@@ -56,9 +58,82 @@ cudaError_t noalloc_scratch(void** out) {
   return cudaSuccess;
 }
 
+// ---------------------------------------------------------------------------------------
+// CUDA IPC for the gathered N-split: a rank exports the allocation holding its output buffer
+// and the other ranks map it.  The handle names the whole cudaMalloc allocation, so the
+// buffer's offset inside it travels with the handle.
+// ---------------------------------------------------------------------------------------
+using GetAddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+GetAddressRangeFn address_range_fn() {
+  static GetAddressRangeFn fn = []() -> GetAddressRangeFn {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &ptr, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<GetAddressRangeFn>(ptr);
+  }();
+  return fn;
+}
+
+std::mutex g_ipc_mu;
+std::map<uintptr_t, void*> g_ipc_open;   // pointer handed out -> mapped allocation base
+
 }  // namespace
 
 extern "C" {
+
+int blackhole_sm100_ipc_get_handle(const void* ptr, void* handle, int64_t* offset) {
+  if (!ptr || !handle || !offset) return static_cast<int>(cudaErrorInvalidValue);
+  GetAddressRangeFn range = address_range_fn();
+  if (!range) return static_cast<int>(cudaErrorNotSupported);
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return static_cast<int>(cudaErrorInvalidValue);
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return static_cast<int>(e);
+  std::memcpy(handle, &h, sizeof(h));
+  *offset = static_cast<int64_t>(reinterpret_cast<uintptr_t>(ptr) - static_cast<uintptr_t>(base));
+  return 0;
+}
+
+int blackhole_sm100_ipc_open(const void* handle, int64_t offset, void** ptr) {
+  if (!handle || !ptr || offset < 0) return static_cast<int>(cudaErrorInvalidValue);
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  void* p = static_cast<uint8_t*>(base) + offset;
+  std::lock_guard<std::mutex> lock(g_ipc_mu);
+  g_ipc_open[reinterpret_cast<uintptr_t>(p)] = base;
+  *ptr = p;
+  return 0;
+}
+
+int blackhole_sm100_ipc_close(void* ptr) {
+  void* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_ipc_mu);
+    auto it = g_ipc_open.find(reinterpret_cast<uintptr_t>(ptr));
+    if (it == g_ipc_open.end()) return static_cast<int>(cudaErrorInvalidValue);
+    base = it->second;
+    g_ipc_open.erase(it);
+  }
+  return static_cast<int>(cudaIpcCloseMemHandle(base));
+}
+
+int blackhole_sm100_nvfp4_bf16_gemm_gather(int M, int N, int K, const void* A, const void* SFA,
+                                           const void* B, const void* SFB, void* const* dst,
+                                           int ndst, int64_t col0, int64_t ldd, float alpha,
+                                           cudaStream_t stream) {
+  return static_cast<int>(blackhole::sm100::nvfp4_bf16_gemm_gather(
+      M, N, K, A, SFA, B, SFB, dst, ndst, col0, ldd, alpha, stream));
+}
 
 int blackhole_sm100_nvfp4_bf16_gemm(int M, int N, int K, const void* A, const void* SFA,
                                     const void* B, const void* SFB, void* D, float alpha,

@@ -3,7 +3,10 @@
 Rank r of P owns rows [r*N/P, (r+1)*N/P) of B (the GEMM's N dimension) and the matching
 scale factors; A and its scale factors are replicated.  Each rank runs the single-GPU
 operator on (M, N/P, K) and produces an M x N/P slice of D; no GPU reads another GPU's
-memory.  An optional all-gather assembles the slices as [P][M][N/P].
+memory.  The slices are assembled either by an NCCL all-gather after the GEMM ([P][M][N/P],
+`nsplit_gemm(gather=True)`), or inside the GEMM itself (`GatheredOutput` +
+`nsplit_gemm_gathered`): every rank's kernel writes its tiles straight into every rank's
+row-major M x N buffer over NVLink while it computes the next tiles.
 
 Because a shard is a whole number of 128-row blocks, its SFB is one contiguous byte range of
 the full SFB tensor (the 128x4 layout advances along K inside a row block, then to the next
@@ -80,3 +83,61 @@ def nsplit_gemm(M: int, N: int, K: int, A, SFA, B, SFB, alpha: float, rank: int,
     out = torch.empty((world, M, s.rows), dtype=torch.bfloat16, device=A.device)
     dist.all_gather_into_tensor(out, D, group=group)
     return assemble(out, world)
+
+
+class GatheredOutput:
+    """A row-major M x N BF16 buffer on every rank, mapped into every other rank (CUDA IPC).
+
+    Collective: every rank of `group` constructs it with the same M and N.  `dst` lists the
+    destinations of this rank's gather call: its own buffer first, then the peers' mappings.
+    """
+
+    def __init__(self, M: int, N: int, rank: int, world: int, group=None):
+        import torch
+        import torch.distributed as dist
+
+        import blackhole_b200 as bh
+
+        self.M, self.N, self.rank, self.world = M, N, rank, world
+        self.out = torch.empty((M, N), dtype=torch.bfloat16, device=torch.cuda.current_device())
+        self._peers = []
+        handles = [None] * world
+        if world > 1:
+            dist.all_gather_object(handles, bh.ipc_get_handle(self.out), group=group)
+            for q in range(world):
+                if q != rank:
+                    self._peers.append(bh.ipc_open(*handles[q]))
+        self.dst = [self.out] + self._peers
+        self._flag = torch.zeros(1, dtype=torch.int32, device=self.out.device)
+        self.group = group
+
+    def barrier(self):
+        """Stream-ordered: returns once every rank's GEMM before it (hence every write into any
+        rank's buffer) has completed, as seen from this rank's stream."""
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(self._flag, group=self.group)
+
+    def close(self):
+        import blackhole_b200 as bh
+
+        for p in self._peers:
+            bh.ipc_close(p)
+        self._peers = []
+        self.dst = [self.out]
+
+
+def nsplit_gemm_gathered(M: int, N: int, K: int, A, SFA, B, SFB, alpha: float, rank: int,
+                         world: int, out: GatheredOutput, stream=None):
+    """This rank's N-slice with the gather fused into the GEMM: afterwards (and after the
+    barrier it ends with) every rank's `out.out` holds the whole row-major M x N result."""
+    import blackhole_b200 as bh
+
+    if out.M != M or out.N != N:
+        raise ValueError("GatheredOutput was made for another shape")
+    s = shard(N, K, rank, world)
+    b, sfb = shard_views(B, SFB, N, K, rank, world)
+    bh.nvfp4_bf16_gemm_gather(M, s.rows, K, A, SFA, b, sfb, out.dst, s.row0, N, alpha,
+                              stream=stream)
+    out.barrier()
+    return out.out

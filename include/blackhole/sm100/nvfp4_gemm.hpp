@@ -163,6 +163,36 @@ inline cudaError_t mxfp4_bf16_gemm(int M, int N, int K, void const* A, void cons
                             stream);
 }
 
+// GEMM with the output gathered in the same kernel: the M x N result goes to columns
+// [col0, col0 + N) of each of the ndst row-major BF16 buffers dst[0..ndst) (rows ldd
+// elements apart).  dst[0] is this GPU's buffer; the others are typically other GPUs' buffers
+// mapped into this process (CUDA IPC), written tile by tile with plain stores over NVLink
+// while the next tiles are computed.  Used by the N-split: rank r of P passes every rank's
+// buffer and col0 = r * N, so each GPU ends with the whole row-major M x (P*N) result.  The
+// call orders nothing across GPUs: the caller synchronises the ranks after it (and before
+// reusing a buffer another rank still reads).  Runs the two-SM schedule for every M.
+inline cudaError_t nvfp4_bf16_gemm_gather(int M, int N, int K, void const* A, void const* SFA,
+                                          void const* B, void const* SFB, void* const* dst,
+                                          int ndst, int64_t col0, int64_t ldd, float alpha,
+                                          cudaStream_t stream = nullptr) {
+  if (!dst || ndst < 1 || ndst > kMaxGatherPeers + 1) return cudaErrorInvalidValue;
+  cudaError_t e = nvfp4_check_args(M, N, K, A, SFA, B, SFB, dst[0]);
+  if (e != cudaSuccess) return e;
+  for (int i = 0; i < ndst; ++i)
+    if (!dst[i] || (reinterpret_cast<uintptr_t>(dst[i]) & 15u)) return cudaErrorInvalidValue;
+  if (col0 < 0 || col0 % 8 != 0 || ldd % 8 != 0 || col0 + N > ldd) return cudaErrorInvalidValue;
+  if (static_cast<int64_t>(M) * ldd > (int64_t(1) << 46)) return cudaErrorInvalidValue;
+  detail::DeviceState* st = detail::prepare_device();
+  if (!st) return cudaErrorInvalidDevice;
+  if (st->init_err != cudaSuccess) return st->init_err;
+  int dev = 0;
+  e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const detail::GatherSpec g{dst, ndst, col0, ldd};
+  return detail::launch_2sm<Nvfp4Gemm2SmTraitsT<256, 5, Nvfp4Format>>(
+      M, N, K, A, SFA, B, SFB, dst[0], alpha, st, dev, stream, &g);
+}
+
 //   A_packed : E2M1, M x K, K-contiguous (two per byte, low nibble first)
 //   SFA      : UE4M3 in the 128x4 layout (make_layout_SFA(M, K)), sf_storage_bytes(M, K) bytes
 //   B_packed : E2M1, N x K, K-contiguous

@@ -84,6 +84,8 @@ using Nvfp4Gemm2SmTraits = Nvfp4Gemm2SmTraitsT<256, 5>;
 
 #if defined(__CUDACC__)
 
+constexpr int kMaxGatherPeers = 7;   // eight GPUs of one node
+
 struct Nvfp4Gemm2SmParams {
   CUtensorMap tmap_a;     // A  [M][K/2] bytes, box 128 x 128 B, 128B swizzle
   CUtensorMap tmap_b;     // B  [N][K/2] bytes, box 128 x 128 B, 128B swizzle
@@ -97,6 +99,13 @@ struct Nvfp4Gemm2SmParams {
   int k_tiles;
   int sf_k_atoms;
   int sf_tail;            // K % 256 != 0: tmap_sfa / tmap_sfb are atom-granular (y = atom)
+  // Gather mode: every output tile is also written, with plain 16-byte stores, to up to
+  // kMaxGatherPeers further row-major buffers (another GPU's memory mapped into this process,
+  // or local memory); peer_d[i] points at this call's first column in buffer i, rows ldd
+  // elements apart.  num_peers = 0 is the ordinary GEMM.
+  int num_peers;
+  int64_t ldd;
+  uint8_t* peer_d[kMaxGatherPeers];
 };
 
 namespace detail {
@@ -359,11 +368,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
           tma_store_2d(&p.tmap_d, box, col0 + 64 * u, row0, pol_d);
           bulk_commit_group();
         }
+        if (p.num_peers > 0) {
+          // the same box to every further buffer: 8 lanes per 128-byte row segment
+#pragma unroll 1
+          for (int it = 0; it < 8; ++it) {
+            const int r = it * 4 + (lane >> 3);
+            const int ch = lane & 7;
+            const int grow = row0 + r;
+            const int gcol = col0 + 64 * u + 8 * ch;
+            if (grow < p.M && gcol < p.N) {
+              const uint4 v = ld_shared_v4(box + r * 128 + ((ch ^ (r & 7)) << 4));
+              const int64_t off = (int64_t(grow) * p.ldd + gcol) * 2;
+              for (int q = 0; q < p.num_peers; ++q)
+                *reinterpret_cast<uint4*>(p.peer_d[q] + off) = v;
+            }
+          }
+        }
       };
       stage_store(v0, v1, 0);
       stage_store(v2, v3, 1);
     }
     if (lane == 0) bulk_wait_group<0>();
+    if (p.num_peers > 0) __threadfence_system();
     __syncwarp();
   }
 
@@ -379,10 +405,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
 
 namespace detail {
 
+// Destinations of a gather-mode call: dst[0] is this GPU's buffer (written by TMA stores),
+// dst[1..n-1] further buffers (plain stores); every buffer is row-major with rows ldd
+// elements apart and receives this call's M x N result at columns [col0, col0 + N).
+struct GatherSpec {
+  void* const* dst;
+  int ndst;
+  int64_t col0;
+  int64_t ldd;
+};
+
 template <class KT>
 inline cudaError_t launch_2sm(int M, int N, int K, const void* A, const void* SFA, const void* B,
                               const void* SFB, void* D, float alpha, DeviceState* st, int dev,
-                              cudaStream_t stream) {
+                              cudaStream_t stream, const GatherSpec* g = nullptr) {
   cudaError_t e = set_smem_once(nvfp4_gemm_2sm_kernel<KT>, KT::SmemBytes, dev);
   if (e != cudaSuccess) return e;
   Nvfp4Gemm2SmParams p;
@@ -398,7 +434,18 @@ inline cudaError_t launch_2sm(int M, int N, int K, const void* A, const void* SF
   e = p.sf_tail ? make_sf_tmap_atoms(&p.tmap_sfb, SFB, N, K, 2, KT::SfAtoms, KT::SFVecSize)
                 : make_sf_tmap_ktile(&p.tmap_sfb, SFB, N, K, 2, 1, KT::SfAtoms, KT::SFVecSize);
   if (e != cudaSuccess) return e;
-  e = make_d_tmap(&p.tmap_d, D, M, N);
+  p.num_peers = 0;
+  p.ldd = N;
+  if (g) {
+    uint8_t* own = static_cast<uint8_t*>(g->dst[0]) + g->col0 * 2;
+    e = make_d_tmap(&p.tmap_d, own, M, N, 64, g->ldd);
+    p.num_peers = g->ndst - 1;
+    p.ldd = g->ldd;
+    for (int i = 0; i < kMaxGatherPeers; ++i)
+      p.peer_d[i] = i + 1 < g->ndst ? static_cast<uint8_t*>(g->dst[i + 1]) + g->col0 * 2 : nullptr;
+  } else {
+    e = make_d_tmap(&p.tmap_d, D, M, N);
+  }
   if (e != cudaSuccess) return e;
   p.status = st->status;
   p.alpha = alpha;

@@ -212,12 +212,13 @@ inline cudaError_t make_sf_tmap_atoms_uncached(CUtensorMap* m, const void* base,
 // Row-major BF16 [rows][cols] output with a (32 rows x box_cols columns) box: the store box
 // of one epilogue warp.  Parts of a box past the tensor edge are not written.
 // box_cols = 64 (128-byte rows, 128B swizzle) or 16 (32-byte rows, 32B swizzle).
+// ld: elements between consecutive rows (>= cols; 0 means cols).
 inline cudaError_t make_d_tmap_uncached(CUtensorMap* m, void* base, int64_t rows, int64_t cols,
-                                        uint32_t box_cols) {
+                                        uint32_t box_cols, int64_t ld = 0) {
   EncodeTiledFn enc = encode_tiled_fn();
   if (!enc) return cudaErrorNotSupported;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * 2)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>((ld > 0 ? ld : cols) * 2)};
   cuuint32_t box[2] = {box_cols, 32u};
   cuuint32_t estr[2] = {1u, 1u};
   const CUtensorMapSwizzle swz = box_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B
@@ -257,10 +258,11 @@ inline cudaError_t make_sf_tmap_atoms(CUtensorMap* m, const void* base, int64_t 
   });
 }
 inline cudaError_t make_d_tmap(CUtensorMap* m, void* base, int64_t rows, int64_t cols,
-                               uint32_t box_cols = 64) {
-  return cached_tmap({2, base, rows, cols, box_cols, 0}, m, [&](CUtensorMap* o) {
-    return make_d_tmap_uncached(o, base, rows, cols, box_cols);
-  });
+                               uint32_t box_cols = 64, int64_t ld = 0) {
+  return cached_tmap({2, base, rows, cols, box_cols, static_cast<uint32_t>(ld)}, m,
+                     [&](CUtensorMap* o) {
+                       return make_d_tmap_uncached(o, base, rows, cols, box_cols, ld);
+                     });
 }
 
 struct DeviceState {

@@ -15,7 +15,7 @@
 extern "C" {
 #endif
 
-#define BLACKHOLE_SM100_ABI_VERSION 2
+#define BLACKHOLE_SM100_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define BLACKHOLE_SM100_API __attribute__((visibility("default")))
@@ -105,6 +105,31 @@ BLACKHOLE_SM100_API int blackhole_sm100_nvfp4_bf16_gemm_noalloc(int M, int N, in
                                                                 const void* SFA, const void* B,
                                                                 const void* SFB, void* D,
                                                                 float alpha, cudaStream_t stream);
+
+/* GEMM with the N-split's all-gather fused in (no counterpart in the reference, whose
+ * multi-GPU path is the caller's NCCL all-gather of [P][M][N/P] slices): the M x N result goes
+ * to columns [col0, col0 + N) of each of the ndst row-major BF16 buffers dst[0..ndst), rows
+ * ldd elements apart.  dst[0] must be this GPU's memory (written by TMA stores); dst[1..] are
+ * written tile by tile with 16-byte stores while later tiles compute -- other GPUs' buffers
+ * mapped with blackhole_sm100_ipc_open, or local memory.  1 <= ndst <= 8, col0 % 8 == 0,
+ * ldd % 8 == 0, col0 + N <= ldd, all dst 16-byte aligned; shapes as blackhole_sm100_nvfp4_bf16_gemm.
+ * Asynchronous on `stream`; nothing orders it against other GPUs: the caller synchronises the
+ * ranks after the call (e.g. a one-element NCCL all-reduce on the same stream) before any rank
+ * reads its buffer, and before a call overwrites a buffer another rank may still read. */
+BLACKHOLE_SM100_API int blackhole_sm100_nvfp4_bf16_gemm_gather(int M, int N, int K, const void* A,
+                                                               const void* SFA, const void* B,
+                                                               const void* SFB, void* const* dst,
+                                                               int ndst, int64_t col0, int64_t ldd,
+                                                               float alpha, cudaStream_t stream);
+
+/* CUDA IPC for those buffers (no counterpart in the reference).  get_handle writes the
+ * 64-byte cudaIpcMemHandle_t of the cudaMalloc allocation that holds ptr, and ptr's offset
+ * inside it; open maps such a handle from another process on this device and returns the
+ * mapped address of the same byte (peer access enabled); close unmaps a pointer open returned. */
+BLACKHOLE_SM100_API int blackhole_sm100_ipc_get_handle(const void* ptr, void* handle,
+                                                       int64_t* offset);
+BLACKHOLE_SM100_API int blackhole_sm100_ipc_open(const void* handle, int64_t offset, void** ptr);
+BLACKHOLE_SM100_API int blackhole_sm100_ipc_close(void* ptr);
 
 /* Self-test of the bounded-wait protocol (no counterpart in the reference): one CTA whose
  * "producer" warp waits limit_ns on a barrier nothing arrives on, gives up, raises the CTA

@@ -34,7 +34,7 @@ def test_library_exports_every_declared_symbol():
     L = bh.load()
     for s in syms:
         assert hasattr(L, s)
-    assert L.blackhole_sm100_abi_version() == 2
+    assert L.blackhole_sm100_abi_version() == 3
     assert "blackhole_sm100_mxfp4_bf16_gemm_ex" in syms and "blackhole_sm100_mxfp4_quantize" in syms
 
 
@@ -79,3 +79,29 @@ def test_null_and_misaligned_pointers_rejected():
         with pytest.raises(bh.BlackholeError) as ei:
             bh.nvfp4_bf16_gemm(128, 128, 256, *args, 1.0, stream=0)
         assert ei.value.code == 1
+
+
+@pytest.mark.parametrize("ndst,col0,ldd,N", [(0, 0, 256, 256), (9, 0, 256, 256), (2, 4, 264, 256),
+                                             (2, 0, 260, 256), (2, 8, 256, 256), (2, -8, 256, 256),
+                                             (2, 0, 256, 100)])
+def test_gather_bad_arguments_rejected_before_launch(ndst, col0, ldd, N):
+    good = 1 << 20
+    with pytest.raises(bh.BlackholeError) as ei:
+        bh.nvfp4_bf16_gemm_gather(128, N, 256, good, good, good, good, [good] * ndst, col0, ldd,
+                                  1.0, stream=0)
+    assert ei.value.code == 1
+
+
+def test_gather_misaligned_destination_rejected():
+    good = 1 << 20
+    with pytest.raises(bh.BlackholeError) as ei:
+        bh.nvfp4_bf16_gemm_gather(128, 256, 256, good, good, good, good, [good, good + 8], 0, 256,
+                                  1.0, stream=0)
+    assert ei.value.code == 1
+
+
+def test_ipc_helpers_reject_null_arguments():
+    L = bh.load()
+    assert L.blackhole_sm100_ipc_get_handle(None, None, None) == 1
+    assert L.blackhole_sm100_ipc_open(None, 0, None) == 1
+    assert L.blackhole_sm100_ipc_close(12345) == 1
