@@ -113,6 +113,22 @@ int64_t bho_sf_storage_bytes_vs(int64_t MN, int64_t K, int vs) {
   return ((MN + 127) / 128) * ((K / vs + 3) / 4) * 512;
 }
 
+/* Signed E4M3 (OCP E4M3FN: bias 7, 3 mantissa bits, subnormal step 2^-9, max 448, no
+ * infinities, 0x7F / 0xFF NaN): round to nearest even on |x| as for UE4M3, finite values
+ * past 448 and infinities saturate to +-448, NaN becomes 0x7F (sign dropped), the sign of
+ * zero and of values that round to zero is kept.  The conventions of
+ * cutlass::float_e4m3_t(float) in CUTLASS 4.5.0 and of the satfinite e4m3 conversion. */
+uint8_t bho_e4m3_from_float(float x) {
+  if (isnan(x)) return 0x7F;
+  uint8_t sign = (uint8_t)((f2u(x) >> 31) << 7);
+  return (uint8_t)(sign | bho_ue4m3_from_float(x));
+}
+
+float bho_e4m3_to_float(uint8_t code) {
+  float v = bho_ue4m3_to_float((uint8_t)(code & 0x7F));
+  return (code & 0x80) ? -v : v;
+}
+
 /* UE8M0: an 8-bit biased exponent, value 2^(code - 127); code 0xFF is NaN. */
 float bho_ue8m0_to_float(uint8_t code) {
   if (code == 0xFF) return NAN;
@@ -224,11 +240,45 @@ void bho_quantize_mxfp4(const float* X, int64_t rows, int64_t K, uint8_t* packed
   }
 }
 
+/* MXFP8 (E4M3 elements) with the same rule: emax_elem = 8 (448 = 1.75 * 2^8), so the
+ * shared exponent is floor(log2 amax) - 8 and scaled elements stay below 2^9; those past
+ * 448 saturate. */
+void bho_quantize_mxfp8(const float* X, int64_t rows, int64_t K, uint8_t* q, uint8_t* sf) {
+  for (int64_t r = 0; r < rows; ++r) {
+    for (int64_t b = 0; b < K / 32; ++b) {
+      const float* x = X + r * K + b * 32;
+      float amax_b = 0.0f;
+      for (int i = 0; i < 32; ++i) {
+        float a = fabsf(x[i]);
+        if (a > amax_b) amax_b = a;
+      }
+      int ebits = (int)((f2u(amax_b) >> 23) & 0xFF);
+      int e = ebits == 0 ? -127 : (ebits - 127) - 8;
+      if (e < -127) e = -127;
+      if (e > 127) e = 127;
+      sf[bho_sf_offset_vs(r, b, K, 32)] = (uint8_t)(e + 127);
+      const float inv = u2f((uint32_t)(127 - e) << 23);
+      for (int i = 0; i < 32; ++i) q[r * K + b * 32 + i] = bho_e4m3_from_float(x[i] * inv);
+    }
+  }
+}
+
 /* ------------------------------------------------------------------------------------ */
 /* Host reference GEMM (example/nvfp4_bf16_gemm.cu:161-168, plus alpha).                  */
+/* Formats: 0 NVFP4 x NVFP4, 1 MXFP4 x MXFP4, 2 MXFP8 (A, one byte per element) x MXFP4.  */
 /* ------------------------------------------------------------------------------------ */
+/* Operand element kinds: 0 NVFP4, 1 MXFP4, 2 MXFP8. */
+static int a_kind(int fmt) { return fmt; }
+static int b_kind(int fmt) { return fmt == 2 ? 1 : fmt; }
+
 static void dequant_row_fmt(int fmt, const uint8_t* P, const uint8_t* SF, int64_t row,
                             int64_t K, float* out) {
+  if (fmt == 2) {
+    const uint8_t* p = P + row * K;
+    for (int64_t k = 0; k < K; ++k)
+      out[k] = bho_e4m3_to_float(p[k]) * bho_ue8m0_to_float(SF[bho_sf_offset_vs(row, k / 32, K, 32)]);
+    return;
+  }
   const uint8_t* p = P + row * (K / 2);
   for (int64_t k = 0; k < K; k += 2) {
     uint8_t byte = p[k / 2];
@@ -275,7 +325,7 @@ static void* gemm_worker(void* arg) {
   float* arow = (float*)malloc(sizeof(float) * (size_t)j->K);
   if (!j->sampled) {
     for (int64_t m = j->m0; m < j->m1; ++m) {
-      dequant_row_fmt(j->fmt, j->A, j->SFA, m, j->K, arow);
+      dequant_row_fmt(a_kind(j->fmt), j->A, j->SFA, m, j->K, arow);
       for (int64_t n = 0; n < j->N; ++n) {
         double ad;
         float acc = dot_seq(arow, j->Bdq + n * j->K, j->K, &ad);
@@ -286,8 +336,8 @@ static void* gemm_worker(void* arg) {
   } else {
     float* brow = (float*)malloc(sizeof(float) * (size_t)j->K);
     for (int64_t s = j->m0; s < j->m1; ++s) {
-      dequant_row_fmt(j->fmt, j->A, j->SFA, j->ms[s], j->K, arow);
-      dequant_row_fmt(j->fmt, j->B, j->SFB, j->ns[s], j->K, brow);
+      dequant_row_fmt(a_kind(j->fmt), j->A, j->SFA, j->ms[s], j->K, arow);
+      dequant_row_fmt(b_kind(j->fmt), j->B, j->SFB, j->ns[s], j->K, brow);
       double ad;
       float acc = dot_seq(arow, brow, j->K, &ad);
       j->D[s] = bho_bf16_from_float(j->alpha * acc);
@@ -355,7 +405,7 @@ void bho_gemm_ref_full_fmt(int fmt, int64_t M, int64_t N, int64_t K, const uint8
                            const uint8_t* SFA, const uint8_t* B, const uint8_t* SFB, float alpha,
                            uint16_t* D, double* absdot, int nthreads) {
   float* Bdq = (float*)malloc(sizeof(float) * (size_t)(N * K));
-  dequant_rows_parallel(fmt, B, SFB, N, K, Bdq, nthreads);
+  dequant_rows_parallel(b_kind(fmt), B, SFB, N, K, Bdq, nthreads);
   gemm_job job = {M, N, K, A, SFA, B, SFB, alpha, D, absdot, Bdq, 0, 0, 0, NULL, NULL, 0, fmt};
   run_jobs(&job, M, nthreads);
   free(Bdq);

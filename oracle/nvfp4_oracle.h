@@ -87,7 +87,14 @@ int64_t bho_sf_storage_bytes_vs(int64_t MN, int64_t K, int vs);
  * e2m1(x * 2^-e_b) (exact scaling, RNE, saturating to 6).  K % 32 == 0; sf zero-filled
  * first by the caller. */
 void bho_quantize_mxfp4(const float* X, int64_t rows, int64_t K, uint8_t* packed, uint8_t* sf);
+/* Signed E4M3 (OCP E4M3FN): RNE, satfinite to +-448, NaN -> 0x7F; decode (0x7F/0xFF NaN). */
+uint8_t bho_e4m3_from_float(float x);
+float   bho_e4m3_to_float(uint8_t code);
+/* MXFP8 quantiser (E4M3 elements, one UE8M0 scale per 32, shared exponent
+ * floor(log2 amax) - 8): q rows*K bytes, sf bho_sf_storage_bytes_vs(rows, K, 32) bytes. */
+void bho_quantize_mxfp8(const float* X, int64_t rows, int64_t K, uint8_t* q, uint8_t* sf);
 /* The reference GEMM for a format: fmt 0 = NVFP4 (as above), 1 = MXFP4. */
+/* fmt: 0 NVFP4 x NVFP4, 1 MXFP4 x MXFP4, 2 MXFP8 A (rows*K bytes) x MXFP4 B. */
 void bho_gemm_ref_full_fmt(int fmt, int64_t M, int64_t N, int64_t K, const uint8_t* A,
                            const uint8_t* SFA, const uint8_t* B, const uint8_t* SFB, float alpha,
                            uint16_t* D, double* absdot, int nthreads);

@@ -72,6 +72,12 @@ def lib():
         L.bho_sf_storage_bytes_vs.argtypes = [c_i64, c_i64, ctypes.c_int]
         L.bho_quantize_mxfp4.restype = None
         L.bho_quantize_mxfp4.argtypes = [c_ptr, c_i64, c_i64, c_ptr, c_ptr]
+        L.bho_e4m3_from_float.restype = ctypes.c_uint8
+        L.bho_e4m3_from_float.argtypes = [ctypes.c_float]
+        L.bho_e4m3_to_float.restype = ctypes.c_float
+        L.bho_e4m3_to_float.argtypes = [ctypes.c_uint8]
+        L.bho_quantize_mxfp8.restype = None
+        L.bho_quantize_mxfp8.argtypes = [c_ptr, c_i64, c_i64, c_ptr, c_ptr]
         L.bho_gemm_ref_full_fmt.restype = None
         L.bho_gemm_ref_full_fmt.argtypes = [ctypes.c_int, c_i64, c_i64, c_i64, c_ptr, c_ptr, c_ptr,
                                             c_ptr, ctypes.c_float, c_ptr, c_ptr, ctypes.c_int]
@@ -147,7 +153,7 @@ def quantize(X: np.ndarray):
     return packed, sf, float(g)
 
 
-FORMATS = {"nvfp4": 0, "mxfp4": 1}
+FORMATS = {"nvfp4": 0, "mxfp4": 1, "mxf8f4": 2}   # mxf8f4: MXFP8 A x MXFP4 B
 
 
 def sf_storage_bytes_vs(mn: int, k: int, vs: int) -> int:
@@ -166,6 +172,17 @@ def quantize_mxfp4(X: np.ndarray):
     sf = np.zeros(sf_storage_bytes_vs(rows, k, 32), dtype=np.uint8)
     lib().bho_quantize_mxfp4(_p(X), rows, k, _p(packed), _p(sf))
     return packed, sf
+
+
+def quantize_mxfp8(X: np.ndarray):
+    """MXFP8 (E4M3)-quantise a (rows, K) float32 matrix (K % 32 == 0): returns (q u8 [rows*K],
+    sf u8)."""
+    X = np.ascontiguousarray(X, dtype=np.float32)
+    rows, k = X.shape
+    q = np.zeros(rows * k, dtype=np.uint8)
+    sf = np.zeros(sf_storage_bytes_vs(rows, k, 32), dtype=np.uint8)
+    lib().bho_quantize_mxfp8(_p(X), rows, k, _p(q), _p(sf))
+    return q, sf
 
 
 def gemm_full(M, N, K, A, SFA, B, SFB, alpha=1.0, nthreads=0, want_absdot=True, fmt="nvfp4"):
