@@ -18,7 +18,8 @@ __all__ = [
     "device_status", "BlackholeError", "nvfp4_quantize", "quantize_tensor",
     "nvfp4_bf16_gemm_ex", "workspace_bytes", "SCHEDULES", "nvfp4_bf16_gemm_noalloc",
     "selftest_bounded_wait", "mxfp4_bf16_gemm", "mxfp4_sf_storage_bytes", "mxfp4_quantize",
-    "quantize_tensor_mxfp4", "nvfp4_bf16_gemm_gather", "ipc_get_handle", "ipc_open", "ipc_close",
+    "quantize_tensor_mxfp4", "mxf8f4_bf16_gemm", "mxfp8_quantize", "quantize_tensor_mxfp8",
+    "nvfp4_bf16_gemm_gather", "ipc_get_handle", "ipc_open", "ipc_close",
 ]
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -63,6 +64,13 @@ def load():
     L.blackhole_sm100_mxfp4_bf16_gemm_ex.restype = i32
     L.blackhole_sm100_mxfp4_bf16_gemm_ex.argtypes = [i32, i32, i32, vp, vp, vp, vp, vp, ctypes.c_float,
                                                      i32, vp, i64, vp]
+    L.blackhole_sm100_mxf8f4_bf16_gemm.restype = i32
+    L.blackhole_sm100_mxf8f4_bf16_gemm.argtypes = [i32, i32, i32, vp, vp, vp, vp, vp, ctypes.c_float, vp]
+    L.blackhole_sm100_mxf8f4_bf16_gemm_ex.restype = i32
+    L.blackhole_sm100_mxf8f4_bf16_gemm_ex.argtypes = [i32, i32, i32, vp, vp, vp, vp, vp,
+                                                      ctypes.c_float, i32, vp, i64, vp]
+    L.blackhole_sm100_mxfp8_quantize.restype = i32
+    L.blackhole_sm100_mxfp8_quantize.argtypes = [vp, i32, i32, i32, vp, vp, vp]
     L.blackhole_sm100_mxfp4_sf_storage_bytes.restype = i64
     L.blackhole_sm100_mxfp4_sf_storage_bytes.argtypes = [i64, i64]
     L.blackhole_sm100_mxfp4_quantize.restype = i32
@@ -168,6 +176,42 @@ def mxfp4_bf16_gemm(M: int, N: int, K: int, A, SFA, B, SFB, D, alpha: float = 1.
         int(workspace_bytes), _stream(stream))
     if rc != 0:
         raise BlackholeError("blackhole_sm100_mxfp4_bf16_gemm_ex", rc)
+
+
+def mxf8f4_bf16_gemm(M: int, N: int, K: int, A, SFA, B, SFB, D, alpha: float = 1.0, stream=None,
+                     schedule: str = "auto", workspace=None, workspace_bytes: int = 0) -> None:
+    """D = bf16(alpha * A . B^T) with A MXFP8 (E4M3, one byte per element) and B MXFP4 (packed
+    E2M1), UE8M0 scales per 32 along K on both (mxfp4_sf_storage_bytes(M|N, K) bytes each).
+    K % 128 == 0; otherwise the shapes, schedules and errors of nvfp4_bf16_gemm_ex."""
+    if workspace is not None and hasattr(workspace, "numel") and not workspace_bytes:
+        workspace_bytes = workspace.numel() * workspace.element_size()
+    rc = load().blackhole_sm100_mxf8f4_bf16_gemm_ex(
+        int(M), int(N), int(K), _ptr(A), _ptr(SFA), _ptr(B), _ptr(SFB), _ptr(D), float(alpha),
+        SCHEDULES[schedule], _ptr(workspace) if workspace is not None else None,
+        int(workspace_bytes), _stream(stream))
+    if rc != 0:
+        raise BlackholeError("blackhole_sm100_mxf8f4_bf16_gemm_ex", rc)
+
+
+def mxfp8_quantize(X, rows: int, K: int, q, sf, x_is_bf16: bool = False, stream=None) -> None:
+    """Quantise X (rows x K, FP32 or BF16, K % 32 == 0) to MXFP8 (E4M3) on the GPU."""
+    rc = load().blackhole_sm100_mxfp8_quantize(
+        _ptr(X), 1 if x_is_bf16 else 0, int(rows), int(K), _ptr(q), _ptr(sf), _stream(stream))
+    if rc != 0:
+        raise BlackholeError("blackhole_sm100_mxfp8_quantize", rc)
+
+
+def quantize_tensor_mxfp8(X, stream=None):
+    """MXFP8 version of quantize_tensor: returns (q uint8 [rows, K], sf uint8)."""
+    import torch
+
+    if X.dim() != 2 or X.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("X must be a 2-D float32 or bfloat16 tensor")
+    rows, K = X.shape
+    q = torch.empty((rows, K), dtype=torch.uint8, device=X.device)
+    sf = torch.empty(mxfp4_sf_storage_bytes(rows, K), dtype=torch.uint8, device=X.device)
+    mxfp8_quantize(X, rows, K, q, sf, x_is_bf16=(X.dtype == torch.bfloat16), stream=stream)
+    return q, sf
 
 
 def mxfp4_sf_storage_bytes(mn: int, k: int) -> int:

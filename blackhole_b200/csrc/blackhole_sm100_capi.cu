@@ -169,6 +169,30 @@ int blackhole_sm100_mxfp4_bf16_gemm_ex(int M, int N, int K, const void* A, const
       workspace, workspace_bytes, stream));
 }
 
+int blackhole_sm100_mxf8f4_bf16_gemm(int M, int N, int K, const void* A, const void* SFA,
+                                     const void* B, const void* SFB, void* D, float alpha,
+                                     cudaStream_t stream) {
+  return static_cast<int>(blackhole::sm100::mxf8f4_bf16_gemm_ex(
+      M, N, K, A, SFA, B, SFB, D, alpha, blackhole::sm100::Nvfp4Schedule::kAuto, nullptr, 0,
+      stream));
+}
+
+int blackhole_sm100_mxf8f4_bf16_gemm_ex(int M, int N, int K, const void* A, const void* SFA,
+                                        const void* B, const void* SFB, void* D, float alpha,
+                                        int schedule, void* workspace, int64_t workspace_bytes,
+                                        cudaStream_t stream) {
+  if (schedule < 0 || schedule > 4) return static_cast<int>(cudaErrorInvalidValue);
+  return static_cast<int>(blackhole::sm100::mxf8f4_bf16_gemm_ex(
+      M, N, K, A, SFA, B, SFB, D, alpha, static_cast<blackhole::sm100::Nvfp4Schedule>(schedule),
+      workspace, workspace_bytes, stream));
+}
+
+int blackhole_sm100_mxfp8_quantize(const void* X, int x_is_bf16, int rows, int K, void* q,
+                                   void* sf, cudaStream_t stream) {
+  return static_cast<int>(
+      blackhole::sm100::mxfp8_quantize(X, x_is_bf16, rows, K, q, sf, stream));
+}
+
 int64_t blackhole_sm100_mxfp4_sf_storage_bytes(int64_t mn, int64_t k) {
   if (mn < 0 || k < 0) return -1;
   return blackhole::sf_storage_bytes_vs(mn, k, 32);

@@ -103,6 +103,8 @@ inline cudaError_t block_scaled_bf16_gemm_ex(int M, int N, int K, void const* A,
                                              int64_t workspace_bytes, cudaStream_t stream) {
   cudaError_t e = nvfp4_check_args(M, N, K, A, SFA, B, SFB, D);
   if (e != cudaSuccess) return e;
+  e = detail::format_check_args<Fmt>(K, B);
+  if (e != cudaSuccess) return e;
   detail::DeviceState* st = detail::prepare_device();
   if (!st) return cudaErrorInvalidDevice;
   if (st->init_err != cudaSuccess) return st->init_err;
@@ -115,11 +117,11 @@ inline cudaError_t block_scaled_bf16_gemm_ex(int M, int N, int K, void const* A,
                           : Nvfp4Schedule::kTwoSm;
   switch (schedule) {
     case Nvfp4Schedule::kOneSm:
-      return detail::launch_1sm<Nvfp4GemmTraitsT<256, 4, Fmt>>(M, N, K, A, SFA, B, SFB, D, alpha,
-                                                                st, dev, stream);
+      return detail::launch_1sm<Nvfp4GemmTraitsT<4, Fmt>>(M, N, K, A, SFA, B, SFB, D, alpha, st,
+                                                           dev, stream);
     case Nvfp4Schedule::kTwoSm:
-      return detail::launch_2sm<Nvfp4Gemm2SmTraitsT<256, 5, Fmt>>(M, N, K, A, SFA, B, SFB, D,
-                                                                   alpha, st, dev, stream);
+      return detail::launch_2sm<Nvfp4Gemm2SmTraitsT<5, Fmt>>(M, N, K, A, SFA, B, SFB, D, alpha,
+                                                              st, dev, stream);
     case Nvfp4Schedule::kSkinny:
     case Nvfp4Schedule::kSkinnyNoPrefetch: {
       if (M > 128) return cudaErrorInvalidValue;
@@ -156,6 +158,17 @@ inline cudaError_t mxfp4_bf16_gemm_ex(int M, int N, int K, void const* A, void c
   return block_scaled_bf16_gemm_ex<Mxfp4Format>(M, N, K, A, SFA, B, SFB, D, alpha, schedule,
                                                 workspace, workspace_bytes, stream);
 }
+// MXFP8 x MXFP4: A (M x K) is E4M3, one byte per element, with UE8M0 scales per 32; B (N x K)
+// is packed E2M1 (MXFP4); both scale tensors in the 128x4 layout with 32-element groups.
+// tcgen05.mma kind::mxf8f6f4 (half the FP4 rate).  Shapes as nvfp4_bf16_gemm plus
+// K % 128 == 0 and B 32-byte aligned.
+inline cudaError_t mxf8f4_bf16_gemm_ex(int M, int N, int K, void const* A, void const* SFA,
+                                       void const* B, void const* SFB, void* D, float alpha,
+                                       Nvfp4Schedule schedule, void* workspace,
+                                       int64_t workspace_bytes, cudaStream_t stream) {
+  return block_scaled_bf16_gemm_ex<Mxf8f4Format>(M, N, K, A, SFA, B, SFB, D, alpha, schedule,
+                                                 workspace, workspace_bytes, stream);
+}
 inline cudaError_t mxfp4_bf16_gemm(int M, int N, int K, void const* A, void const* SFA,
                                    void const* B, void const* SFB, void* D, float alpha = 1.0f,
                                    cudaStream_t stream = nullptr) {
@@ -189,7 +202,7 @@ inline cudaError_t nvfp4_bf16_gemm_gather(int M, int N, int K, void const* A, vo
   e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   const detail::GatherSpec g{dst, ndst, col0, ldd};
-  return detail::launch_2sm<Nvfp4Gemm2SmTraitsT<256, 5, Nvfp4Format>>(
+  return detail::launch_2sm<Nvfp4Gemm2SmTraitsT<5, Nvfp4Format>>(
       M, N, K, A, SFA, B, SFB, dst[0], alpha, st, dev, stream, &g);
 }
 

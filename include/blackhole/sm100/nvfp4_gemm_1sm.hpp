@@ -26,25 +26,29 @@ namespace blackhole::sm100 {
 // =====================================================================================
 // 1. Compile-time configuration
 // =====================================================================================
-template <int TileK_ = 256, int Stages_ = 4, class Fmt_ = Nvfp4Format>
+template <int Stages_ = 4, class Fmt_ = Nvfp4Format>
 struct Nvfp4GemmTraitsT {
   using Fmt = Fmt_;
+  using Geo = BlockScaleGeometry<Fmt>;
   static constexpr int SFVecSize = Fmt::SfVec;   // elements per scale factor (16 or 32)
 
   static constexpr int TileM = 128;              // UMMA M (one CTA, TMEM lanes)
   static constexpr int TileN = 256;              // UMMA N
-  static constexpr int TileK = TileK_;           // elements per k-tile (256 = 128 B rows)
-  static constexpr int MmaK = 64;                // elements per tcgen05.mma (32 bytes)
-  static constexpr int KSteps = TileK / MmaK;    // 4 MMAs per k-tile
+  static constexpr int TileK = Fmt::TileK;       // elements per k-tile (128-byte smem rows)
+  static constexpr int KSteps = Geo::KSteps;     // 4 MMAs per k-tile
   static constexpr int Stages = Stages_;
 
-  static constexpr int RowBytes = TileK / 2;                        // 128 or 64
+  static constexpr int RowBytes = Geo::RowBytes;                    // 128
   static constexpr int ABytes = TileM * RowBytes;                   // 16 KB
   static constexpr int BBytes = TileN * RowBytes;                   // 32 KB
-  // 512-byte scale-factor atoms per 128 rows and k-tile: 4 (NVFP4) or 2 (MXFP4); k-step j
-  // reads atom j / StepsPerAtom at byte pair 2 * (j % StepsPerAtom) of each entry.
-  static constexpr int StepsPerAtom = SFVecSize / 16;
-  static constexpr int SfAtoms = KSteps / StepsPerAtom;
+  // bytes the A / B loads of a k-tile complete on the stage barrier (global bytes: an
+  // expanded 4-bit B fills twice its size in shared memory)
+  static constexpr int ATx = TileM * Geo::ARowTx;
+  static constexpr int BTx = TileN * Geo::BRowTx;
+  // 512-byte scale-factor atoms per 128 rows and k-tile: 4 (NVFP4), 2 (MXFP4), 1 (MXFP8 x
+  // MXFP4); k-step j reads atom j / StepsPerAtom from scale-factor ID Geo::sf_id(j).
+  static constexpr int StepsPerAtom = Geo::StepsPerAtom;
+  static constexpr int SfAtoms = Geo::SfAtoms;
   static constexpr int SFABytes = (TileM / 128) * SfAtoms * 512;    // 2 KB (NVFP4)
   static constexpr int SFBBytes = (TileN / 128) * SfAtoms * 512;    // 4 KB (NVFP4)
   static constexpr int StageBytes = ABytes + BBytes + SFABytes + SFBBytes;
@@ -76,7 +80,7 @@ struct Nvfp4GemmTraitsT {
   static_assert(SmemBytes <= arch_traits<Arch::kSm100>::max_smem_per_cta, "smem budget");
   static_assert(SfCol + 2 * SfStride <= TmemCols, "TMEM budget");
 };
-using Nvfp4GemmTraits = Nvfp4GemmTraitsT<256, 4>;
+using Nvfp4GemmTraits = Nvfp4GemmTraitsT<4>;
 
 #if defined(__CUDACC__)
 
@@ -194,7 +198,7 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
         detail::tile_coords<KT>(tile, p, m_blk, n_blk);
         const bool sfb_hi = (2 * n_blk + 1) < p.n_blocks128;
         const uint32_t bytes =
-            KT::ABytes + KT::BBytes + KT::SFABytes +
+            KT::ATx + KT::BTx + KT::SFABytes +
             ((sfb_hi || p.sf_tail) ? KT::SFBBytes : KT::SFBBytes / 2);
         const uint8_t* sfa_src = p.sfa + (int64_t(m_blk) * p.sf_k_atoms) * 512;
         const uint8_t* sfb_src0 = p.sfb + (int64_t(2 * n_blk) * p.sf_k_atoms) * 512;
@@ -245,7 +249,8 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
     // ------------------------------ MMA issuer --------------------------------------
     // Per k-tile: probe the next stage's barrier, copy this stage's scale factors to TMEM,
     // four MMAs, commit, then consume the probe (falling back to a bounded wait).
-    constexpr uint32_t idesc = idesc_bs(KT::TileM, KT::TileN, KT::Fmt::ScaleType);
+    constexpr uint32_t idesc = idesc_block_scaled(KT::TileM, KT::TileN, KT::Fmt::AFormat,
+                                                  KT::Fmt::BFormat, KT::Fmt::ScaleType);
     int stage = 0;
     uint32_t phase = 0;
     uint32_t acc_phase = 0;
@@ -289,8 +294,8 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
         for (int j = 0; j < KT::KSteps; ++j) {
           // +32 bytes of K per step inside the swizzled row (descriptor units: 16 B)
           const int at = j / KT::StepsPerAtom;
-          const uint32_t sid = 2u * uint32_t(j % KT::StepsPerAtom);   // byte in the entry
-          tc_mma_nvf4_w<KT::SFVecSize>(
+          const uint32_t sid = KT::Geo::sf_id(j);   // byte in the entry
+          tc_mma_bs_w<typename KT::Fmt>(
               tmem + KT::AccCol, adesc + 2 * j, bdesc + 2 * j, idesc_with_sf_id(idesc, sid),
               sf_tmem_addr(ta + 4 * at, sid), sf_tmem_addr(ta + 4 * KT::SfAtoms + 8 * at, sid),
               (kt | j) != 0 ? 1u : 0u);
@@ -404,9 +409,9 @@ inline cudaError_t launch_1sm(int M, int N, int K, const void* A, const void* SF
   cudaError_t e = set_smem_once(nvfp4_gemm_kernel<KT>, KT::SmemBytes, dev);
   if (e != cudaSuccess) return e;
   Nvfp4GemmParams p;
-  e = make_kmajor_tmap(&p.tmap_a, A, M, K / 2, KT::TileM, KT::RowBytes);
+  e = make_a_tmap<typename KT::Fmt>(&p.tmap_a, A, M, K, KT::TileM);
   if (e != cudaSuccess) return e;
-  e = make_kmajor_tmap(&p.tmap_b, B, N, K / 2, KT::TileN, KT::RowBytes);
+  e = make_b_tmap<typename KT::Fmt>(&p.tmap_b, B, N, K, KT::TileN);
   if (e != cudaSuccess) return e;
   e = make_d_tmap(&p.tmap_d, D, M, N, 16);
   if (e != cudaSuccess) return e;

@@ -33,27 +33,31 @@
 
 namespace blackhole::sm100 {
 
-template <int TileK_ = 256, int Stages_ = 5, class Fmt_ = Nvfp4Format>
+template <int Stages_ = 5, class Fmt_ = Nvfp4Format>
 struct Nvfp4Gemm2SmTraitsT {
   using Fmt = Fmt_;
+  using Geo = BlockScaleGeometry<Fmt>;
   static constexpr int SFVecSize = Fmt::SfVec;
   static constexpr int TileM = 256;              // per pair (UMMA M)
   static constexpr int CtaM = 128;
   static constexpr int TileN = 256;              // UMMA N
   static constexpr int CtaN = 128;               // B rows held per CTA
-  static constexpr int TileK = TileK_;
-  static constexpr int KSteps = TileK / 64;
+  static constexpr int TileK = Fmt::TileK;       // elements per k-tile (128-byte smem rows)
+  static constexpr int KSteps = Geo::KSteps;
   static constexpr int Stages = Stages_;
 
-  static constexpr int RowBytes = TileK / 2;
+  static constexpr int RowBytes = Geo::RowBytes;
   static constexpr int ABytes = CtaM * RowBytes;           // 16 KB
   static constexpr int BBytes = CtaN * RowBytes;           // 16 KB
-  // scale-factor atoms per 128 rows and k-tile: 4 (NVFP4) or 2 (MXFP4)
-  static constexpr int StepsPerAtom = SFVecSize / 16;
-  static constexpr int SfAtoms = KSteps / StepsPerAtom;
+  static constexpr int ATx = CtaM * Geo::ARowTx;           // global bytes per k-tile
+  static constexpr int BTx = CtaN * Geo::BRowTx;
+  // scale-factor atoms per 128 rows and k-tile: 4 (NVFP4), 2 (MXFP4), 1 (MXFP8 x MXFP4)
+  static constexpr int StepsPerAtom = Geo::StepsPerAtom;
+  static constexpr int SfAtoms = Geo::SfAtoms;
   static constexpr int SFABytes = SfAtoms * 512;           // 2 KB NVFP4 (own 128 rows)
   static constexpr int SFBBytes = 2 * SfAtoms * 512;       // 4 KB NVFP4 (all 256 rows)
   static constexpr int StageBytes = ABytes + BBytes + SFABytes + SFBBytes;
+  static constexpr int StageTx = ATx + BTx + SFABytes + SFBBytes;
 
   static constexpr int NumWarps = 10;
   static constexpr int NumThreads = NumWarps * 32;
@@ -78,9 +82,8 @@ struct Nvfp4Gemm2SmTraitsT {
   static constexpr int RasterGroupM = 8;         // in 256-row tiles
 
   static_assert(SmemBytes <= arch_traits<Arch::kSm100>::max_smem_per_cta, "smem budget");
-  static_assert(TileK == 256, "scale factors are fetched as one 2 KB row per block and k-tile");
 };
-using Nvfp4Gemm2SmTraits = Nvfp4Gemm2SmTraitsT<256, 5>;
+using Nvfp4Gemm2SmTraits = Nvfp4Gemm2SmTraitsT<5>;
 
 #if defined(__CUDACC__)
 
@@ -209,7 +212,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
             break;
           }
           const uint32_t lb = mapa_shared(full_bar(stage), 0);
-          if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), 2u * KT::StageBytes);
+          if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), 2u * KT::StageTx);
           tma_load_2d_pair(sA + stage * KT::ABytes, &p.tmap_a, lb, kt * KT::RowBytes, a_row, pol);
           tma_load_2d_pair(sB + stage * KT::BBytes, &p.tmap_b, lb, kt * KT::RowBytes, b_row, pol);
           // one request per operand: SFA as one 2 KB row, SFB as the pair's two 2 KB rows
@@ -237,7 +240,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
     // Per k-tile: probe the next stage's barrier, copy this stage's scale factors to TMEM,
     // four MMAs, commit, then consume the probe (falling back to a bounded wait).
     if (rank == 0) {
-      constexpr uint32_t idesc = idesc_bs(KT::TileM, KT::TileN, KT::Fmt::ScaleType);
+      constexpr uint32_t idesc = idesc_block_scaled(KT::TileM, KT::TileN, KT::Fmt::AFormat,
+                                                    KT::Fmt::BFormat, KT::Fmt::ScaleType);
       const uint32_t acc_full_0 = mapa_shared(acc_full, 0);
       const uint32_t acc_full_1 = mapa_shared(acc_full, 1);
       int stage = 0;
@@ -282,8 +286,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
 #pragma unroll
           for (int j = 0; j < KT::KSteps; ++j) {
             const int at = j / KT::StepsPerAtom;
-            const uint32_t sid = 2u * uint32_t(j % KT::StepsPerAtom);   // byte in the entry
-            tc_mma_nvf4_pair_w<KT::SFVecSize>(
+            const uint32_t sid = KT::Geo::sf_id(j);   // byte in the entry
+            tc_mma_bs_pair_w<typename KT::Fmt>(
                 tmem + KT::AccCol, adesc + 2 * j, bdesc + 2 * j, idesc_with_sf_id(idesc, sid),
                 sf_tmem_addr(ta + 4 * at, sid), sf_tmem_addr(ta + 4 * KT::SfAtoms + 8 * at, sid),
                 (kt | j) != 0 ? 1u : 0u);
@@ -326,10 +330,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
       if (!wait_bounded_warp(acc_full, acc_phase, abort_flag, p.status, kStatusEpilogueTimeout)) break;
       tc_fence_after();
       uint32_t v0[32], v1[32], v2[32], v3[32];
-      tmem_ld_32x32b_x32(t_row + 0, v0);
-      tmem_ld_32x32b_x32(t_row + 32, v1);
-      tmem_ld_32x32b_x32(t_row + 64, v2);
-      tmem_ld_32x32b_x32(t_row + 96, v3);
+      // Measured on B200: the two-SM kind::mxf8f6f4 MMA (N = 256) leaves output column n in
+      // accumulator column n XOR 32 (32-column groups swapped pairwise inside each half; lanes
+      // and halves as for kind::mxf4nvf4), so that kind reads the groups crosswise.
+      constexpr uint32_t x = KT::Fmt::Kind == MmaKind::kMxf8f6f4 ? 32u : 0u;
+      tmem_ld_32x32b_x32(t_row + (0 ^ x), v0);
+      tmem_ld_32x32b_x32(t_row + (32 ^ x), v1);
+      tmem_ld_32x32b_x32(t_row + (64 ^ x), v2);
+      tmem_ld_32x32b_x32(t_row + (96 ^ x), v3);
       tmem_ld_wait();
       reg_fence(v0);
       reg_fence(v1);
@@ -422,9 +430,9 @@ inline cudaError_t launch_2sm(int M, int N, int K, const void* A, const void* SF
   cudaError_t e = set_smem_once(nvfp4_gemm_2sm_kernel<KT>, KT::SmemBytes, dev);
   if (e != cudaSuccess) return e;
   Nvfp4Gemm2SmParams p;
-  e = make_kmajor_tmap(&p.tmap_a, A, M, K / 2, KT::CtaM, KT::RowBytes);
+  e = make_a_tmap<typename KT::Fmt>(&p.tmap_a, A, M, K, KT::CtaM);
   if (e != cudaSuccess) return e;
-  e = make_kmajor_tmap(&p.tmap_b, B, N, K / 2, KT::CtaN, KT::RowBytes);
+  e = make_b_tmap<typename KT::Fmt>(&p.tmap_b, B, N, K, KT::CtaN);
   if (e != cudaSuccess) return e;
   // K % 256 != 0: 4 rows of 512 B per block, so that the K tail reads zeros (slower per k-tile)
   p.sf_tail = K % KT::TileK != 0;

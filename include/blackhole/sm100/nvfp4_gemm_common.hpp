@@ -236,6 +236,52 @@ inline cudaError_t make_kmajor_tmap(CUtensorMap* m, const void* base, int64_t ro
     return make_kmajor_tmap_uncached(o, base, rows, row_bytes, box_rows, box_bytes);
   });
 }
+// Packed 4-bit [rows][K] operand read as CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B: every 16
+// values (8 bytes) land in 16 bytes of shared memory, the one-byte-per-element form
+// kind::mxf8f6f4 reads.  Box: 128 elements (a 128-byte smem row, 128B swizzle) x box_rows;
+// x coordinates are in elements.  Needs K % 128 == 0 and a 32-byte aligned base.
+inline cudaError_t make_fp4_expand_tmap_uncached(CUtensorMap* m, const void* base, int64_t rows,
+                                                 int64_t k, uint32_t box_rows) {
+  EncodeTiledFn enc = encode_tiled_fn();
+  if (!enc) return cudaErrorNotSupported;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(k / 2)};
+  cuuint32_t box[2] = {128u, box_rows};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 2, const_cast<void*>(base), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+inline cudaError_t make_fp4_expand_tmap(CUtensorMap* m, const void* base, int64_t rows, int64_t k,
+                                        uint32_t box_rows) {
+  return cached_tmap({6, base, rows, k, box_rows, 0}, m, [&](CUtensorMap* o) {
+    return make_fp4_expand_tmap_uncached(o, base, rows, k, box_rows);
+  });
+}
+// Operand maps of a format: 128-byte boxes of box_rows rows per k-tile.
+template <class Fmt>
+inline cudaError_t make_a_tmap(CUtensorMap* m, const void* A, int64_t rows, int64_t k,
+                               uint32_t box_rows) {
+  return make_kmajor_tmap(m, A, rows, k * Fmt::ABits / 8, box_rows);
+}
+template <class Fmt>
+inline cudaError_t make_b_tmap(CUtensorMap* m, const void* B, int64_t rows, int64_t k,
+                               uint32_t box_rows) {
+  if constexpr (Fmt::BExpand)
+    return make_fp4_expand_tmap(m, B, rows, k, box_rows);
+  else
+    return make_kmajor_tmap(m, B, rows, k * Fmt::BBits / 8, box_rows);
+}
+// Shapes and alignment a format adds to nvfp4_check_args: the expanded 4-bit B needs
+// K % 128 == 0 (a whole k-tile) and a 32-byte aligned base.
+template <class Fmt>
+inline cudaError_t format_check_args(int K, const void* B) {
+  if constexpr (Fmt::BExpand) {
+    if (K % 128 != 0 || (reinterpret_cast<uintptr_t>(B) & 31u)) return cudaErrorInvalidValue;
+  }
+  return cudaSuccess;
+}
 inline cudaError_t make_sf_tmap(CUtensorMap* m, const void* base, int64_t mn, int64_t k,
                                 uint32_t box_atoms = 4) {
   return cached_tmap({1, base, mn, k, box_atoms, 0}, m, [&](CUtensorMap* o) {

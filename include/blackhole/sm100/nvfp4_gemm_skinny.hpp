@@ -38,19 +38,22 @@ namespace blackhole::sm100 {
 template <int MPAD_, class Fmt_ = Nvfp4Format>
 struct Nvfp4SkinnyTraits {
   using Fmt = Fmt_;
+  using Geo = BlockScaleGeometry<Fmt>;
   static constexpr int SFVecSize = Fmt::SfVec;
   static constexpr int MPAD = MPAD_;            // UMMA N
   static constexpr int TileW = 128;             // rows of B per unit (UMMA M)
-  static constexpr int TileK = 256;
-  static constexpr int KSteps = 4;
-  static constexpr int RowBytes = 128;
+  static constexpr int TileK = Fmt::TileK;      // elements per k-tile (128-byte smem rows)
+  static constexpr int KSteps = Geo::KSteps;
+  static constexpr int RowBytes = Geo::RowBytes;
   static constexpr int WBytes = TileW * RowBytes;           // 16 KB
   static constexpr int XBytes = MPAD * RowBytes;            // 2..16 KB
-  // scale-factor atoms per 128 rows and k-tile: 4 (NVFP4) or 2 (MXFP4)
-  static constexpr int StepsPerAtom = SFVecSize / 16;
-  static constexpr int SfAtoms = KSteps / StepsPerAtom;
+  // scale-factor atoms per 128 rows and k-tile: 4 (NVFP4), 2 (MXFP4), 1 (MXFP8 x MXFP4)
+  static constexpr int StepsPerAtom = Geo::StepsPerAtom;
+  static constexpr int SfAtoms = Geo::SfAtoms;
   static constexpr int SFBytes = SfAtoms * 512;             // 2 KB per operand (NVFP4)
   static constexpr int StageBytes = WBytes + XBytes + 2 * SFBytes;
+  // global bytes a stage's loads complete (the expanded 4-bit B is half its smem size)
+  static constexpr int StageTx = TileW * Geo::BRowTx + MPAD * Geo::ARowTx + 2 * SFBytes;
   static constexpr int Stages = (MPAD <= 32) ? 9 : (MPAD == 64 ? 8 : 6);
   // k-tiles of B prefetched into L2 before the dependency wait (beyond the smem stages)
   static constexpr int L2PrefetchKTiles = 20;
@@ -301,7 +304,7 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
           }
           const uint32_t fb = full_bar(stage);
           const int64_t k_off = int64_t(kt) * KT::SfAtoms * 512;
-          mbar_arrive_expect_tx(fb, KT::StageBytes);
+          mbar_arrive_expect_tx(fb, KT::StageTx);
           // A (small, L2-resident) ahead of B in the copy engine's queue
           tma_load_2d(st_x(stage), &p.tmap_x, fb, kt * KT::RowBytes, 0, pol_x);
           if (p.sf_tail)  // atoms past K read zeros
@@ -331,7 +334,9 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
     }
   } else if (warp == KT::MmaWarp) {
     // ------------------------------ MMA issuer --------------------------------------
-    constexpr uint32_t idesc = idesc_bs(128, MPAD, KT::Fmt::ScaleType);
+    // swap-AB: the MMA's A operand is the weights (B), its B operand the activations (A)
+    constexpr uint32_t idesc = idesc_block_scaled(128, MPAD, KT::Fmt::BFormat, KT::Fmt::AFormat,
+                                                  KT::Fmt::ScaleType);
     int stage = 0;
     uint32_t phase = 0;
     int acc = 0;
@@ -367,8 +372,8 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
 #pragma unroll
           for (int j = 0; j < KT::KSteps; ++j) {
             const int at = j / KT::StepsPerAtom;
-            const uint32_t sid = 2u * uint32_t(j % KT::StepsPerAtom);   // byte in the entry
-            tc_mma_nvf4_w<KT::SFVecSize>(
+            const uint32_t sid = KT::Geo::sf_id(j);   // byte in the entry
+            tc_mma_bs_w<typename KT::Fmt>(
                 d_tmem, wdesc + 2 * j, xdesc + 2 * j, idesc_with_sf_id(idesc, sid),
                 sf_tmem_addr(tmem + KT::SfwCol + 4 * at, sid),
                 sf_tmem_addr(tmem + KT::SfxCol + 4 * at, sid), (kt != sg.kt0 || j != 0) ? 1u : 0u);
@@ -531,9 +536,9 @@ inline cudaError_t launch_skinny(int M, int N, int K, const void* A, const void*
   e = set_smem_once(nvfp4_gemm_skinny_kernel<KT>, KT::SmemBytes, dev);
   if (e != cudaSuccess) return e;
   Nvfp4SkinnyParams p;
-  e = make_kmajor_tmap(&p.tmap_w, B, N, K / 2, 128);
+  e = make_b_tmap<typename KT::Fmt>(&p.tmap_w, B, N, K, 128);
   if (e != cudaSuccess) return e;
-  e = make_kmajor_tmap(&p.tmap_x, A, M, K / 2, KT::MPAD);
+  e = make_a_tmap<typename KT::Fmt>(&p.tmap_x, A, M, K, KT::MPAD);
   if (e != cudaSuccess) return e;
   p.kt_per_rb = (K + KT::TileK - 1) / KT::TileK;
   p.sf_tail = K % KT::TileK != 0;
@@ -590,6 +595,8 @@ inline cudaError_t block_scaled_bf16_gemm_skinny(int M, int N, int K, void const
                                                  cudaStream_t stream = nullptr,
                                                  int grid_cap = 1 << 30, bool prefetch = true) {
   cudaError_t e = nvfp4_check_args(M, N, K, A, SFA, B, SFB, D);
+  if (e != cudaSuccess) return e;
+  e = detail::format_check_args<Fmt>(K, B);
   if (e != cudaSuccess) return e;
   if (M > 128 || !workspace || (reinterpret_cast<uintptr_t>(workspace) & 15u))
     return cudaErrorInvalidValue;

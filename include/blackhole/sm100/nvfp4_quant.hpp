@@ -211,6 +211,58 @@ __global__ void __launch_bounds__(256) mx_quantize_kernel(const T* __restrict__ 
   sf[blackhole::sf_offset_vs(r, kg, K, 32)] = static_cast<uint8_t>(code);
 }
 
+// Two floats to two E4M3 bytes (round to nearest even, finite values past 448 saturate):
+// lo in the low byte.
+__device__ __forceinline__ uint32_t e4m3x2_satfinite(float lo, float hi) {
+  uint16_t d;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
+// MXFP8 (OCP MX v1.0, E4M3 elements): as mx_quantize_kernel with the E4M3 element exponent
+// 8, e = floor(log2(amax_b)) - 8, and 32 bytes of E4M3 codes per group.
+template <class T>
+__global__ void __launch_bounds__(256) mx8_quantize_kernel(const T* __restrict__ x, int rows,
+                                                           int K, uint8_t* __restrict__ q,
+                                                           uint8_t* __restrict__ sf) {
+  const int groups = K / 32;
+  const int groups_pad = (groups + 3) / 4 * 4;
+  const int64_t rows_pad = (int64_t(rows) + 127) / 128 * 128;
+  const int64_t idx = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;
+  if (idx >= rows_pad * groups_pad) return;
+  const int64_t r = idx / groups_pad;
+  const int64_t kg = idx - r * groups_pad;
+  uint32_t code = 0;
+  if (r < rows && kg < groups) {
+    float v[32];
+    float lo16[16], hi16[16];
+    load16(x + r * K + kg * 32, lo16);
+    load16(x + r * K + kg * 32 + 16, hi16);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      v[i] = lo16[i];
+      v[16 + i] = hi16[i];
+    }
+    float amax_b = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) amax_b = fmaxf(amax_b, fabsf(v[i]));
+    const int ebits = static_cast<int>((__float_as_uint(amax_b) >> 23) & 0xFFu);
+    int e = ebits == 0 ? -127 : ebits - 135;
+    e = max(-127, min(127, e));
+    code = static_cast<uint32_t>(e + 127);
+    const float inv = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);
+    uint32_t w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      w[i] = e4m3x2_satfinite(v[4 * i] * inv, v[4 * i + 1] * inv) |
+             (e4m3x2_satfinite(v[4 * i + 2] * inv, v[4 * i + 3] * inv) << 16);
+    uint4* dst = reinterpret_cast<uint4*>(q + r * K + kg * 32);
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  }
+  sf[blackhole::sf_offset_vs(r, kg, K, 32)] = static_cast<uint8_t>(code);
+}
+
 }  // namespace quant_detail
 
 // X: rows x K (FP32 if x_is_bf16 == 0, else BF16), K % 16 == 0, 16-byte aligned.
@@ -267,6 +319,27 @@ inline cudaError_t mxfp4_quantize(const void* X, int x_is_bf16, int rows, int K,
     quant_detail::mx_quantize_kernel<<<static_cast<int>(grid), 256, 0, stream>>>(
         static_cast<const float*>(X), rows, K, static_cast<uint8_t*>(packed),
         static_cast<uint8_t*>(sf));
+  return cudaGetLastError();
+}
+
+// MXFP8 quantiser: X rows x K (FP32 if x_is_bf16 == 0, else BF16), K % 32 == 0, 16-byte
+// aligned.  q: rows*K bytes of E4M3 (16-byte aligned).  sf: sf_storage_bytes_vs(rows, K, 32)
+// bytes, every padding byte written 0.
+inline cudaError_t mxfp8_quantize(const void* X, int x_is_bf16, int rows, int K, void* q,
+                                  void* sf, cudaStream_t stream = nullptr) {
+  if (rows < 1 || K < 32 || K % 32 != 0 || !X || !q || !sf) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(X) & 15u) || (reinterpret_cast<uintptr_t>(q) & 15u))
+    return cudaErrorInvalidValue;
+  const int64_t work = (int64_t(rows) + 127) / 128 * 128 * ((K / 32 + 3) / 4 * 4);
+  const int64_t grid = (work + 255) / 256;
+  if (grid > 0x7FFFFFFF) return cudaErrorInvalidValue;
+  if (x_is_bf16)
+    quant_detail::mx8_quantize_kernel<<<static_cast<int>(grid), 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(X), rows, K, static_cast<uint8_t*>(q),
+        static_cast<uint8_t*>(sf));
+  else
+    quant_detail::mx8_quantize_kernel<<<static_cast<int>(grid), 256, 0, stream>>>(
+        static_cast<const float*>(X), rows, K, static_cast<uint8_t*>(q), static_cast<uint8_t*>(sf));
   return cudaGetLastError();
 }
 

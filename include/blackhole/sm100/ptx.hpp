@@ -7,6 +7,8 @@
 
 #include <cstdint>
 
+#include <blackhole/sm100/block_scale_format.hpp>
+
 #if defined(__CUDACC__)
 #include <cuda.h>  // CUtensorMap
 
@@ -286,6 +288,29 @@ __device__ __forceinline__ void tc_mma_nvf4_w(uint32_t d_tmem, uint64_t adesc, u
         : "memory");
   }
 }
+// kind::mxf8f6f4 (one UE8M0 scale per 32 elements, the instruction's only block size).
+__device__ __forceinline__ void tc_mma_f8f6f4_w(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                                uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, P;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync _|P, 0xffffffff;\n\t"
+      "@P tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t"
+      "}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+// The block-scaled MMA of a format (block_scale_format.hpp), one CTA.
+template <class Fmt>
+__device__ __forceinline__ void tc_mma_bs_w(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                            uint32_t accumulate) {
+  if constexpr (Fmt::Kind == MmaKind::kMxf8f6f4)
+    tc_mma_f8f6f4_w(d_tmem, adesc, bdesc, idesc, sfa_tmem, sfb_tmem, accumulate);
+  else
+    tc_mma_nvf4_w<Fmt::SfVec>(d_tmem, adesc, bdesc, idesc, sfa_tmem, sfb_tmem, accumulate);
+}
 __device__ __forceinline__ void tc_commit_w(uint32_t bar) {
   asm volatile(
       "{\n\t.reg .pred P;\n\telect.sync _|P, 0xffffffff;\n\t"
@@ -323,6 +348,28 @@ __device__ __forceinline__ void tc_mma_nvf4_pair_w(uint32_t d_tmem, uint64_t ade
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
         : "memory");
   }
+}
+__device__ __forceinline__ void tc_mma_f8f6f4_pair_w(uint32_t d_tmem, uint64_t adesc,
+                                                     uint64_t bdesc, uint32_t idesc,
+                                                     uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                                     uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, P;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync _|P, 0xffffffff;\n\t"
+      "@P tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t"
+      "}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+template <class Fmt>
+__device__ __forceinline__ void tc_mma_bs_pair_w(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                                 uint32_t idesc, uint32_t sfa_tmem,
+                                                 uint32_t sfb_tmem, uint32_t accumulate) {
+  if constexpr (Fmt::Kind == MmaKind::kMxf8f6f4)
+    tc_mma_f8f6f4_pair_w(d_tmem, adesc, bdesc, idesc, sfa_tmem, sfb_tmem, accumulate);
+  else
+    tc_mma_nvf4_pair_w<Fmt::SfVec>(d_tmem, adesc, bdesc, idesc, sfa_tmem, sfb_tmem, accumulate);
 }
 __device__ __forceinline__ void tc_commit_pair_w(uint32_t cluster_bar) {
   asm volatile(
@@ -495,11 +542,24 @@ __host__ __device__ constexpr uint32_t idesc_nvf4(int m, int n) {
 __host__ __device__ constexpr uint32_t idesc_bs(int m, int n, uint32_t scale_type) {
   return idesc_nvf4(m, n) | (scale_type << 23);
 }
+// General block-scaled descriptor: element formats of the MMA's A and B operands (bits 7-9,
+// 10-12; kind::mxf4nvf4 E2M1 = 1, kind::mxf8f6f4 E4M3 = 0 / E2M1 = 5), scale format (bit 23),
+// N >> 3 (bits 17-22), M >> 4 (bits 24-28); both operands K-major.
+__host__ __device__ constexpr uint32_t idesc_block_scaled(int m, int n, uint32_t a_fmt,
+                                                          uint32_t b_fmt, uint32_t scale_type) {
+  return (a_fmt << 7) | (b_fmt << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (scale_type << 23) | (static_cast<uint32_t>(m >> 4) << 24);
+}
 // Scale-factor byte ID of both operands (bits 29-30 for A, 4-5 for B): which byte of each
 // 32-bit scale-factor column an MMA starts at.  With 32-element blocks an atom (4 bytes per
 // row) serves two 64-element MMAs: the first reads bytes 0-1 (ID 0), the second 2-3 (ID 2).
 __host__ __device__ constexpr uint32_t idesc_with_sf_id(uint32_t idesc, uint32_t id) {
   return idesc | (id << 29) | (id << 4);
+}
+// Separate IDs for A (bits 29-30) and B (bits 4-5).
+__host__ __device__ constexpr uint32_t idesc_with_sf_ids(uint32_t idesc, uint32_t a_id,
+                                                         uint32_t b_id) {
+  return idesc | (a_id << 29) | (b_id << 4);
 }
 // The same byte ID also rides in bits 30-31 of the scale-factor TMEM address operand (the
 // lane field of these addresses is 0; CUTLASS's UMMA atoms pass it the same way).

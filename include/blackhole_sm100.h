@@ -15,7 +15,7 @@
 extern "C" {
 #endif
 
-#define BLACKHOLE_SM100_ABI_VERSION 3
+#define BLACKHOLE_SM100_ABI_VERSION 4
 
 #if defined(__GNUC__)
 #define BLACKHOLE_SM100_API __attribute__((visibility("default")))
@@ -157,6 +157,29 @@ BLACKHOLE_SM100_API int blackhole_sm100_mxfp4_bf16_gemm_ex(int M, int N, int K, 
                                                            int schedule, void* workspace,
                                                            int64_t workspace_bytes,
                                                            cudaStream_t stream);
+/* MXFP8 x MXFP4 -> BF16 (no counterpart in the reference): A (M x K) E4M3, one byte per
+ * element, B (N x K) packed E2M1; one UE8M0 scale per 32 elements along K on both, 128x4
+ * layout with 32-element groups (blackhole_sm100_mxfp4_sf_storage_bytes bytes each).
+ * tcgen05.mma kind::mxf8f6f4.  Shapes and schedules as the MXFP4 calls, plus K % 128 == 0
+ * and B 32-byte aligned. */
+BLACKHOLE_SM100_API int blackhole_sm100_mxf8f4_bf16_gemm(int M, int N, int K, const void* A,
+                                                         const void* SFA, const void* B,
+                                                         const void* SFB, void* D, float alpha,
+                                                         cudaStream_t stream);
+BLACKHOLE_SM100_API int blackhole_sm100_mxf8f4_bf16_gemm_ex(int M, int N, int K, const void* A,
+                                                            const void* SFA, const void* B,
+                                                            const void* SFB, void* D, float alpha,
+                                                            int schedule, void* workspace,
+                                                            int64_t workspace_bytes,
+                                                            cudaStream_t stream);
+/* MXFP8 quantiser (OCP MX v1.0, E4M3 elements, shared exponent floor(log2 amax) - 8, elements
+ * rounded to nearest even and saturated at +-448): X rows x K (FP32 when x_is_bf16 == 0, else
+ * BF16, K % 32 == 0, 16-byte aligned) -> q (rows*K bytes, 16-byte aligned) and sf (MX layout,
+ * padding written 0).  Asynchronous on `stream`. */
+BLACKHOLE_SM100_API int blackhole_sm100_mxfp8_quantize(const void* X, int x_is_bf16, int rows,
+                                                       int K, void* q, void* sf,
+                                                       cudaStream_t stream);
+
 /* Bytes of an (mn, k) MXFP4 scale-factor tensor (rows padded to 128, 32-element groups
  * padded to a multiple of 4); negative on error. */
 BLACKHOLE_SM100_API int64_t blackhole_sm100_mxfp4_sf_storage_bytes(int64_t mn, int64_t k);

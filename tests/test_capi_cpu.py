@@ -34,7 +34,7 @@ def test_library_exports_every_declared_symbol():
     L = bh.load()
     for s in syms:
         assert hasattr(L, s)
-    assert L.blackhole_sm100_abi_version() == 3
+    assert L.blackhole_sm100_abi_version() == 4
     assert "blackhole_sm100_mxfp4_bf16_gemm_ex" in syms and "blackhole_sm100_mxfp4_quantize" in syms
 
 
@@ -105,3 +105,17 @@ def test_ipc_helpers_reject_null_arguments():
     assert L.blackhole_sm100_ipc_get_handle(None, None, None) == 1
     assert L.blackhole_sm100_ipc_open(None, 0, None) == 1
     assert L.blackhole_sm100_ipc_close(12345) == 1
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 256 + 32), (128, 128, 64), (128, 100, 256), (0, 128, 256)])
+def test_mxf8f4_bad_shapes_rejected_before_launch(M, N, K):
+    for sched in ("auto", "1sm", "2sm", "skinny"):
+        with pytest.raises(bh.BlackholeError) as ei:
+            bh.mxf8f4_bf16_gemm(M, N, K, 4096, 4096, 4096, 4096, 4096, 1.0, stream=0, schedule=sched)
+        assert ei.value.code == 1
+
+
+def test_mxf8f4_b_needs_32_byte_alignment():
+    with pytest.raises(bh.BlackholeError) as ei:
+        bh.mxf8f4_bf16_gemm(128, 128, 256, 4096, 4096, 4096 + 16, 4096, 4096, 1.0, stream=0)
+    assert ei.value.code == 1
