@@ -216,6 +216,8 @@ def time_gemm(M, N, K, sets, D, steps, warmup, world, schedule="auto", fmt="nvfp
     def launch(A, SFA, B, SFB, alpha):
         if fmt == "mxfp4":
             bh.mxfp4_bf16_gemm(M, N, K, A, SFA, B, SFB, D, alpha, schedule=schedule)
+        elif fmt == "mxf8f4":
+            bh.mxf8f4_bf16_gemm(M, N, K, A, SFA, B, SFB, D, alpha, schedule=schedule)
         elif schedule == "auto":
             bh.nvfp4_bf16_gemm(M, N, K, A, SFA, B, SFB, D, alpha)
         else:
@@ -430,43 +432,48 @@ def run_decode(args, dev, rank, world, hbm_peak, peak_src, Ms=(16, 1, 64, 128)):
     return out
 
 
-def run_mxfp4(args, dev, rank, world, fp4_peak, hbm_peak):
-    """The MXFP4 sibling (UE8M0 scale per 32) on configs[1]'s and configs[2]'s M=16 shapes,
-    same sources (N(0,1); decode weights N(0, 0.02^2)), quantised on the device."""
+def run_mx(args, dev, rank, world, fp4_peak, hbm_peak, fmt="mxfp4"):
+    """A sibling format on configs[1]'s and configs[2]'s M=16 shapes, same sources (N(0,1);
+    decode weights N(0, 0.02^2)), quantised on the device: "mxfp4" (UE8M0 scale per 32) or
+    "mxf8f4" (MXFP8 activations x MXFP4 weights; kind::mxf8f6f4, half the FP4 MMA rate)."""
     import torch
     import blackhole_b200 as bh
 
-    def mx_operand(rows, K, seed, std):
+    def mx_operand(rows, K, seed, std, fp8=False):
         g = torch.Generator(device=dev)
         g.manual_seed(seed)
         x = torch.randn((rows, K), generator=g, device=dev, dtype=torch.float32)
         if std != 1.0:
             x.mul_(std)
-        packed, sf = bh.quantize_tensor_mxfp4(x)
+        q, sf = bh.quantize_tensor_mxfp8(x) if fp8 else bh.quantize_tensor_mxfp4(x)
         torch.cuda.synchronize()
-        return packed, sf
+        return q, sf
 
+    a8 = fmt == "mxf8f4"
+    peak = fp4_peak / 2 if a8 else fp4_peak
     out = {}
     M = N = K = 8192
-    sets = [mx_operand(M, K, 1 + 7 * i, 1.0) + mx_operand(N, K, 1000 + rank + 7 * i, 1.0) + (1.0,)
+    sets = [mx_operand(M, K, 1 + 7 * i, 1.0, a8) + mx_operand(N, K, 1000 + rank + 7 * i, 1.0) + (1.0,)
             for i in range(4)]
+    set_mb = sum(t.numel() for t in sets[0][:4]) / 1e6
     D = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
     steps = max(10, min(args.steps, 400))
-    tot = time_gemm(M, N, K, sets, D, steps, max(3, args.warmup), world, fmt="mxfp4")
+    tot = time_gemm(M, N, K, sets, D, steps, max(3, args.warmup), world, fmt=fmt)
     ms = max_over_ranks(tot / steps, world)
     tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
     out["gemm_8192"] = {"value": tf * world, "unit": "TFLOP/s", "ms_per_step": ms, "steps": steps,
-                        "roofline_frac": tf / fp4_peak,
-                        "l2": "4 rotating input sets (~290 MB > 126 MB L2), back to back"}
+                        "roofline_frac": tf / peak, "peak": peak,
+                        "l2": f"4 rotating input sets ({set_mb * 4:.0f} MB > 126 MB L2), back to back"}
     del sets, D
     Md, Nd, Kd = 16, 28672, 8192
-    dsets = [mx_operand(Md, Kd, 2 + 7 * i, 1.0) + mx_operand(Nd, Kd, 2000 + rank + 7 * i, 0.02) + (1.0,)
+    dsets = [mx_operand(Md, Kd, 2 + 7 * i, 1.0, a8) + mx_operand(Nd, Kd, 2000 + rank + 7 * i, 0.02) + (1.0,)
              for i in range(3)]
     Dd = torch.empty((Md, Nd), dtype=torch.bfloat16, device=dev)
     dsteps = max(30, min(args.steps, 2000))
-    tot = time_gemm(Md, Nd, Kd, dsets, Dd, dsteps, max(3, args.warmup), world, fmt="mxfp4")
+    tot = time_gemm(Md, Nd, Kd, dsets, Dd, dsteps, max(3, args.warmup), world, fmt=fmt)
     dms = max_over_ranks(tot / dsteps, world)
-    nbytes = Md * Kd // 2 + Nd * Kd // 2 + (Md + Nd) * Kd // 32 + 2 * Md * Nd
+    a_bytes = Md * Kd if a8 else Md * Kd // 2   # MXFP8: one byte per element
+    nbytes = a_bytes + Nd * Kd // 2 + (Md + Nd) * Kd // 32 + 2 * Md * Nd
     gbs = nbytes / (dms * 1e-3) / 1e9
     out["decode_m16"] = {"value": gbs * world, "unit": "GB/s", "ms_per_step": dms, "steps": dsteps,
                          "bytes_per_launch": nbytes, "roofline_frac": gbs / hbm_peak,
@@ -657,8 +664,10 @@ def main():
         result["prefill"] = run_prefill(args, dev, rank, world, fp4_peak)
         result["nsplit"] = run_nsplit(args, dev, rank, world, fp4_peak)
         result["gpu_launches"] += result["prefill"]["steps"] + result["nsplit"]["steps"]
-        result["mxfp4"] = run_mxfp4(args, dev, rank, world, fp4_peak, hbm_peak)
+        result["mxfp4"] = run_mx(args, dev, rank, world, fp4_peak, hbm_peak, "mxfp4")
         result["gpu_launches"] += result["mxfp4"]["steps"]
+        result["mxf8f4"] = run_mx(args, dev, rank, world, fp4_peak, hbm_peak, "mxf8f4")
+        result["gpu_launches"] += result["mxf8f4"]["steps"]
 
     if world > 1 and args.gather:
         import torch.distributed as dist
