@@ -54,7 +54,12 @@ struct Nvfp4SkinnyTraits {
   static constexpr int StageBytes = WBytes + XBytes + 2 * SFBytes;
   // global bytes a stage's loads complete (the expanded 4-bit B is half its smem size)
   static constexpr int StageTx = TileW * Geo::BRowTx + MPAD * Geo::ARowTx + 2 * SFBytes;
-  static constexpr int Stages = (MPAD <= 32) ? 9 : (MPAD == 64 ? 8 : 6);
+  // NVFP4 / MXFP4: depths tuned per width.  An expanded 4-bit B (MXFP8 x MXFP4) moves half
+  // its shared-memory bytes per stage, so its ring takes every stage that fits (at most 12).
+  static constexpr int FitStages =
+      (arch_traits<Arch::kSm100>::max_smem_per_cta - 1024 - 8 * (2 * 12 + 5) - 16) / StageBytes;
+  static constexpr int Stages = Fmt::BExpand ? (FitStages < 12 ? FitStages : 12)
+                                             : ((MPAD <= 32) ? 9 : (MPAD == 64 ? 8 : 6));
   // k-tiles of B prefetched into L2 before the dependency wait (beyond the smem stages)
   static constexpr int L2PrefetchKTiles = 20;
   // ranges by ticket: the first CTA to start gets (1 + s) x, the last (1 - s) x the mean
