@@ -183,7 +183,8 @@ inline cudaError_t mxfp4_bf16_gemm(int M, int N, int K, void const* A, void cons
 // while the next tiles are computed.  Used by the N-split: rank r of P passes every rank's
 // buffer and col0 = r * N, so each GPU ends with the whole row-major M x (P*N) result.  The
 // call orders nothing across GPUs: the caller synchronises the ranks after it (and before
-// reusing a buffer another rank still reads).  Runs the two-SM schedule for every M.
+// reusing a buffer another rank still reads).  M <= 128 runs the skinny schedule (its
+// epilogue stores 2-byte elements to every buffer), larger M the two-SM schedule.
 inline cudaError_t nvfp4_bf16_gemm_gather(int M, int N, int K, void const* A, void const* SFA,
                                           void const* B, void const* SFB, void* const* dst,
                                           int ndst, int64_t col0, int64_t ldd, float alpha,
@@ -202,6 +203,14 @@ inline cudaError_t nvfp4_bf16_gemm_gather(int M, int N, int K, void const* A, vo
   e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   const detail::GatherSpec g{dst, ndst, col0, ldd};
+  if (M <= 128) {   // decode-sized: the skinny schedule, its epilogue storing to every buffer
+    const int64_t need = nvfp4_skinny_workspace_bytes(st->num_sms, nvfp4_skinny_mpad(M));
+    void* ws = nullptr;
+    e = detail::library_workspace(dev, stream, need, &ws);
+    if (e != cudaSuccess) return e;
+    return block_scaled_bf16_gemm_skinny<Nvfp4Format>(M, N, K, A, SFA, B, SFB, dst[0], alpha, ws,
+                                                      need, stream, 1 << 30, true, &g);
+  }
   return detail::launch_2sm<Nvfp4Gemm2SmTraitsT<5, Nvfp4Format>>(
       M, N, K, A, SFA, B, SFB, dst[0], alpha, st, dev, stream, &g);
 }

@@ -98,8 +98,6 @@ using Nvfp4Gemm2SmTraits = Nvfp4Gemm2SmTraitsT<5>;
 
 #if defined(__CUDACC__)
 
-constexpr int kMaxGatherPeers = 7;   // eight GPUs of one node
-
 struct Nvfp4Gemm2SmParams {
   CUtensorMap tmap_a;     // A  [M][K/2] bytes, box 128 x 128 B, 128B swizzle
   CUtensorMap tmap_b;     // B  [N][K/2] bytes, box 128 x 128 B, 128B swizzle
@@ -489,16 +487,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
 }
 
 namespace detail {
-
-// Destinations of a gather-mode call: dst[0] is this GPU's buffer (written by TMA stores),
-// dst[1..n-1] further buffers (plain stores); every buffer is row-major with rows ldd
-// elements apart and receives this call's M x N result at columns [col0, col0 + N).
-struct GatherSpec {
-  void* const* dst;
-  int ndst;
-  int64_t col0;
-  int64_t ldd;
-};
 
 template <class KT>
 inline cudaError_t launch_2sm(int M, int N, int K, const void* A, const void* SFA, const void* B,

@@ -25,6 +25,10 @@
 
 namespace blackhole::sm100 {
 
+// Gather mode (the N-split's all-gather fused into the GEMM): besides this GPU's buffer, up to
+// kMaxGatherPeers further buffers (the other GPUs of an eight-GPU node) receive every tile.
+constexpr int kMaxGatherPeers = 7;
+
 // Status bits written when a bounded wait gives up.
 enum : uint32_t {
   kStatusLoadTimeout = 1u,
@@ -51,6 +55,16 @@ inline cudaError_t nvfp4_check_args(int M, int N, int K, const void* A, const vo
 #if defined(__CUDACC__)
 
 namespace detail {
+
+// Destinations of a gather-mode call: dst[0] is this GPU's buffer, dst[1..ndst) further
+// buffers written with plain stores; every buffer is row-major with rows ldd elements apart
+// and receives the call's M x N result at columns [col0, col0 + N).
+struct GatherSpec {
+  void* const* dst;
+  int ndst;
+  int64_t col0;
+  int64_t ldd;
+};
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);

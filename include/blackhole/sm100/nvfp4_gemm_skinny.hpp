@@ -110,7 +110,10 @@ struct Nvfp4SkinnyParams {
   CUtensorMap tmap_x;   // A [M][K/2] bytes, box MPAD rows x 128 B
   const uint8_t* sfw;   // SFB
   const uint8_t* sfx;   // SFA
-  uint16_t* d;
+  uint16_t* d;          // this call's first output column; rows ldd elements apart
+  int64_t ldd;
+  int num_peers;        // gather mode: further destinations, laid out as d
+  uint16_t* peer_d[kMaxGatherPeers];
   float* ws;            // [grid][MPAD][128] partials
   uint32_t* flags;      // [grid][8]: one per epilogue warp
   uint32_t* ticket;     // entry counter: CTAs take ranges in the order they start
@@ -512,10 +515,14 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
       for (int m = 0; m < EC; ++m) {
         if (m0 + m < p.M && n < p.N) {
           __nv_bfloat16 b = __float2bfloat16_rn(a * v[m]);
-          p.d[int64_t(m0 + m) * p.N + n] = *reinterpret_cast<uint16_t*>(&b);
+          const uint16_t bits = *reinterpret_cast<uint16_t*>(&b);
+          const int64_t off = int64_t(m0 + m) * p.ldd + n;
+          p.d[off] = bits;
+          for (int q = 0; q < p.num_peers; ++q) p.peer_d[q][off] = bits;
         }
       }
     }
+    if (p.num_peers > 0) __threadfence_system();
   }
 
   tc_fence_before();
@@ -534,7 +541,7 @@ inline cudaError_t launch_skinny(int M, int N, int K, const void* A, const void*
                                  const void* SFB, void* D, float alpha, void* ws, int64_t ws_bytes,
                                  int grid_cap, bool prefetch, DeviceState* st, cudaStream_t stream,
                                  int l2_prefetch_ktiles = KT::L2PrefetchKTiles,
-                                 int skew = KT::RangeSkew) {
+                                 int skew = KT::RangeSkew, const GatherSpec* g = nullptr) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -560,6 +567,15 @@ inline cudaError_t launch_skinny(int M, int N, int K, const void* A, const void*
   p.sfw = static_cast<const uint8_t*>(SFB);
   p.sfx = static_cast<const uint8_t*>(SFA);
   p.d = static_cast<uint16_t*>(D);
+  p.ldd = N;
+  p.num_peers = 0;
+  if (g) {
+    p.d = static_cast<uint16_t*>(g->dst[0]) + g->col0;
+    p.ldd = g->ldd;
+    p.num_peers = g->ndst - 1;
+  }
+  for (int i = 0; i < kMaxGatherPeers; ++i)
+    p.peer_d[i] = g && i + 1 < g->ndst ? static_cast<uint16_t*>(g->dst[i + 1]) + g->col0 : nullptr;
   p.flags = static_cast<uint32_t*>(ws);
   p.ticket = p.flags + kSkinnyFlagsPerCta * st->num_sms;
   p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + nvfp4_skinny_flag_bytes(st->num_sms));
@@ -598,7 +614,8 @@ inline cudaError_t block_scaled_bf16_gemm_skinny(int M, int N, int K, void const
                                                  void* D, float alpha, void* workspace,
                                                  int64_t workspace_bytes,
                                                  cudaStream_t stream = nullptr,
-                                                 int grid_cap = 1 << 30, bool prefetch = true) {
+                                                 int grid_cap = 1 << 30, bool prefetch = true,
+                                                 const detail::GatherSpec* g = nullptr) {
   cudaError_t e = nvfp4_check_args(M, N, K, A, SFA, B, SFB, D);
   if (e != cudaSuccess) return e;
   e = detail::format_check_args<Fmt>(K, B);
@@ -611,16 +628,20 @@ inline cudaError_t block_scaled_bf16_gemm_skinny(int M, int N, int K, void const
   switch (nvfp4_skinny_mpad(M)) {
     case 16:
       return detail::launch_skinny<Nvfp4SkinnyTraits<16, Fmt>>(
-          M, N, K, A, SFA, B, SFB, D, alpha, workspace, workspace_bytes, grid_cap, prefetch, st, stream);
+          M, N, K, A, SFA, B, SFB, D, alpha, workspace, workspace_bytes, grid_cap, prefetch, st, stream,
+          Nvfp4SkinnyTraits<16, Fmt>::L2PrefetchKTiles, Nvfp4SkinnyTraits<16, Fmt>::RangeSkew, g);
     case 32:
       return detail::launch_skinny<Nvfp4SkinnyTraits<32, Fmt>>(
-          M, N, K, A, SFA, B, SFB, D, alpha, workspace, workspace_bytes, grid_cap, prefetch, st, stream);
+          M, N, K, A, SFA, B, SFB, D, alpha, workspace, workspace_bytes, grid_cap, prefetch, st, stream,
+          Nvfp4SkinnyTraits<32, Fmt>::L2PrefetchKTiles, Nvfp4SkinnyTraits<32, Fmt>::RangeSkew, g);
     case 64:
       return detail::launch_skinny<Nvfp4SkinnyTraits<64, Fmt>>(
-          M, N, K, A, SFA, B, SFB, D, alpha, workspace, workspace_bytes, grid_cap, prefetch, st, stream);
+          M, N, K, A, SFA, B, SFB, D, alpha, workspace, workspace_bytes, grid_cap, prefetch, st, stream,
+          Nvfp4SkinnyTraits<64, Fmt>::L2PrefetchKTiles, Nvfp4SkinnyTraits<64, Fmt>::RangeSkew, g);
     default:
       return detail::launch_skinny<Nvfp4SkinnyTraits<128, Fmt>>(
-          M, N, K, A, SFA, B, SFB, D, alpha, workspace, workspace_bytes, grid_cap, prefetch, st, stream);
+          M, N, K, A, SFA, B, SFB, D, alpha, workspace, workspace_bytes, grid_cap, prefetch, st, stream,
+          Nvfp4SkinnyTraits<128, Fmt>::L2PrefetchKTiles, Nvfp4SkinnyTraits<128, Fmt>::RangeSkew, g);
   }
 }
 

@@ -109,9 +109,10 @@ BLACKHOLE_SM100_API int blackhole_sm100_nvfp4_bf16_gemm_noalloc(int M, int N, in
 /* GEMM with the N-split's all-gather fused in (no counterpart in the reference, whose
  * multi-GPU path is the caller's NCCL all-gather of [P][M][N/P] slices): the M x N result goes
  * to columns [col0, col0 + N) of each of the ndst row-major BF16 buffers dst[0..ndst), rows
- * ldd elements apart.  dst[0] must be this GPU's memory (written by TMA stores); dst[1..] are
- * written tile by tile with 16-byte stores while later tiles compute -- other GPUs' buffers
- * mapped with blackhole_sm100_ipc_open, or local memory.  1 <= ndst <= 8, col0 % 8 == 0,
+ * ldd elements apart.  dst[0] must be this GPU's memory; dst[1..] are written tile by tile with
+ * plain stores while later tiles compute -- other GPUs' buffers mapped with
+ * blackhole_sm100_ipc_open, or local memory.  M <= 128 runs the skinny (decode) schedule, larger
+ * M the two-SM schedule.  1 <= ndst <= 8, col0 % 8 == 0,
  * ldd % 8 == 0, col0 + N <= ldd, all dst 16-byte aligned; shapes as blackhole_sm100_nvfp4_bf16_gemm.
  * Asynchronous on `stream`; nothing orders it against other GPUs: the caller synchronises the
  * ranks after the call (e.g. a one-element NCCL all-reduce on the same stream) before any rank

@@ -22,7 +22,9 @@ def _bits(t):
 
 
 @pytest.mark.parametrize("M,N,K,world", [(256, 1024, 512, 2), (300, 1024, 768, 4),
-                                         (200, 2048, 256, 8), (1000, 1024, 1024, 2)])
+                                         (200, 2048, 256, 8), (1000, 1024, 1024, 2),
+                                         (16, 2048, 1024, 4), (1, 1024, 512, 2),
+                                         (100, 1024, 768, 8), (128, 4096, 2048, 2)])
 def test_emulated_ranks_all_hold_the_full_result(M, N, K, world):
     import torch
     import blackhole_b200 as bh
@@ -47,18 +49,19 @@ def test_emulated_ranks_all_hold_the_full_result(M, N, K, world):
     assert bad == 0, f"{bad} elements beyond tolerance (max err {maxerr}, err/tol {ratio})"
 
 
-def test_single_destination_equals_plain_gemm_and_respects_columns():
+@pytest.mark.parametrize("M,schedule", [(130, "2sm"), (16, "skinny"), (77, "skinny")])
+def test_single_destination_equals_plain_gemm_and_respects_columns(M, schedule):
     """ndst = 1 writes exactly the plain GEMM's bits into the column window of a wider buffer;
     a ragged window (col0 = 8, N = 264) and ragged M leave every other column untouched."""
     import torch
     import blackhole_b200 as bh
 
-    M, N, K, col0, ldd = 130, 264, 512, 8, 288
+    N, K, col0, ldd = 264, 512, 8, 288
     A, SFA, B, SFB, alpha = C.make_operands(M, N, K, seed=5)
     dev = torch.device("cuda:0")
     tA, tSFA, tB, tSFB = (torch.from_numpy(x).to(dev) for x in (A, SFA, B, SFB))
     plain = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
-    bh.nvfp4_bf16_gemm_ex(M, N, K, tA, tSFA, tB, tSFB, plain, alpha, schedule="2sm")
+    bh.nvfp4_bf16_gemm_ex(M, N, K, tA, tSFA, tB, tSFB, plain, alpha, schedule=schedule)
     wide = [torch.full((M, ldd), 0x1234, dtype=torch.int16, device=dev) for _ in range(3)]
     bh.nvfp4_bf16_gemm_gather(M, N, K, tA, tSFA, tB, tSFB, wide, col0, ldd, alpha)
     torch.cuda.synchronize()

@@ -13,7 +13,7 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
-M, N, K = 512, 2048, 1024
+SHAPES = [(512, 2048, 1024), (16, 4096, 2048)]   # two-SM and skinny (decode) schedules
 
 
 def _free_port():
@@ -38,23 +38,24 @@ def _worker(rank, world, port, errfile):
         dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
                                 world_size=world, timeout=datetime.timedelta(seconds=60),
                                 device_id=torch.device("cuda", rank))
-        A, SFA, B, SFB, alpha = C.make_operands(M, N, K, seed=21)
         dev = torch.device("cuda", rank)
-        tA, tSFA, tB, tSFB = (torch.from_numpy(x).to(dev) for x in (A, SFA, B, SFB))
-        out = GatheredOutput(M, N, rank, world)
-        out.out.fill_(float("nan"))
-        out.barrier()
-        for _ in range(2):
-            nsplit_gemm_gathered(M, N, K, tA, tSFA, tB, tSFB, alpha, rank, world, out)
-        torch.cuda.synchronize()
-        assert bh.device_status(rank) == 0
-        got = out.out.view(torch.int16).cpu().numpy().view(np.uint16)
-        ref, ad = O.gemm_full(M, N, K, A, SFA, B, SFB, alpha)
-        bad, maxerr, ratio, _ = O.check(ref, got, alpha, K, ad)
-        assert bad == 0, f"rank {rank}: {bad} bad (max err {maxerr}, err/tol {ratio})"
-        out.barrier()
-        torch.cuda.synchronize()
-        out.close()
+        for M, N, K in SHAPES:
+            A, SFA, B, SFB, alpha = C.make_operands(M, N, K, seed=21 + M)
+            tA, tSFA, tB, tSFB = (torch.from_numpy(x).to(dev) for x in (A, SFA, B, SFB))
+            out = GatheredOutput(M, N, rank, world)
+            out.out.fill_(float("nan"))
+            out.barrier()
+            for _ in range(2):
+                nsplit_gemm_gathered(M, N, K, tA, tSFA, tB, tSFB, alpha, rank, world, out)
+            torch.cuda.synchronize()
+            assert bh.device_status(rank) == 0
+            got = out.out.view(torch.int16).cpu().numpy().view(np.uint16)
+            ref, ad = O.gemm_full(M, N, K, A, SFA, B, SFB, alpha)
+            bad, maxerr, ratio, _ = O.check(ref, got, alpha, K, ad)
+            assert bad == 0, f"rank {rank} {M}x{N}x{K}: {bad} bad (max err {maxerr}, err/tol {ratio})"
+            out.barrier()
+            torch.cuda.synchronize()
+            out.close()
         dist.barrier()
         dist.destroy_process_group()
     except BaseException as exc:  # reported to the parent through the file
