@@ -571,7 +571,58 @@ def run_nsplit(args, dev, rank, world, fp4_peak):
         go.close()
         del go
     del A, SFA, B, SFB, D
+    if world > 1:
+        out["decode_gather"] = run_decode_gather(dev, rank, world)
+        out["steps"] += out["decode_gather"]["steps"]
     return out
+
+
+def run_decode_gather(dev, rank, world, steps=50):
+    """Tensor-parallel decode: configs[2]'s M=16, K=8192 GEMM with the N=28672 weights split
+    over the ranks and the output all-gathered, per step either GEMM + NCCL all-gather
+    ([P][M][N/P]) or the gather fused into the skinny GEMM + its one-element all-reduce
+    barrier (row-major M x N on every GPU)."""
+    import torch
+    import torch.distributed as dist
+    import blackhole_b200 as bh
+    from blackhole_b200.nsplit import GatheredOutput, shard
+
+    M, N, K = 16, 28672, 8192
+    sh = shard(N, K, rank, world)
+    A, SFA, sa = make_operand(M, K, 2, 1.0, dev)
+    B, SFB, sb = make_operand(sh.rows, K, 2000 + rank, 0.02, dev)
+    alpha = float(sa[1].item() * sb[1].item())
+    D = torch.empty((M, sh.rows), dtype=torch.bfloat16, device=dev)
+    g = torch.empty((world, M, sh.rows), dtype=torch.bfloat16, device=dev)
+    go = GatheredOutput(M, N, rank, world)
+
+    def nccl_step():
+        bh.nvfp4_bf16_gemm(M, sh.rows, K, A, SFA, B, SFB, D, alpha)
+        dist.all_gather_into_tensor(g, D)
+
+    def fused_step():
+        bh.nvfp4_bf16_gemm_gather(M, sh.rows, K, A, SFA, B, SFB, go.dst, sh.row0, N, alpha)
+        go.barrier()
+
+    res = {}
+    for name, step in (("gemm_then_nccl", nccl_step), ("fused", fused_step)):
+        for _ in range(5):
+            step()
+        barrier(world)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(steps):
+            step()
+        e.record()
+        barrier(world)
+        res[name] = max_over_ranks(s.elapsed_time(e) / steps, world) * 1e3
+    go.close()
+    del A, SFA, B, SFB, D, g, go
+    return {"workload": f"M={M} N={N} K={K}, N split over {world} GPUs, output all-gathered",
+            "us_per_step_gemm_then_nccl": res["gemm_then_nccl"], "us_per_step_fused": res["fused"],
+            "speedup": res["gemm_then_nccl"] / res["fused"], "steps": 2 * steps,
+            "note": "each step includes its cross-GPU synchronisation (the all-gather, or the "
+                    "fused path's one-element all-reduce)"}
 
 
 # ---------------------------------------------------------------------------------------
