@@ -532,17 +532,7 @@ __device__ __forceinline__ uint64_t desc_sf_atom(uint32_t saddr) {
   return d;
 }
 
-// Instruction descriptor of kind::mxf4nvf4: E2M1 A and B (format 1), both K-major,
-// UE4M3 scales (scale format 0), FP32 accumulation, M x N tile.
-__host__ __device__ constexpr uint32_t idesc_nvf4(int m, int n) {
-  return (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
-         (static_cast<uint32_t>(m >> 4) << 24);
-}
-// With the scale-factor format (bit 23: 0 = UE4M3, 1 = UE8M0).
-__host__ __device__ constexpr uint32_t idesc_bs(int m, int n, uint32_t scale_type) {
-  return idesc_nvf4(m, n) | (scale_type << 23);
-}
-// General block-scaled descriptor: element formats of the MMA's A and B operands (bits 7-9,
+// Block-scaled instruction descriptor: element formats of the MMA's A and B operands (bits 7-9,
 // 10-12; kind::mxf4nvf4 E2M1 = 1, kind::mxf8f6f4 E4M3 = 0 / E2M1 = 5), scale format (bit 23),
 // N >> 3 (bits 17-22), M >> 4 (bits 24-28); both operands K-major.
 __host__ __device__ constexpr uint32_t idesc_block_scaled(int m, int n, uint32_t a_fmt,
@@ -551,18 +541,15 @@ __host__ __device__ constexpr uint32_t idesc_block_scaled(int m, int n, uint32_t
          (scale_type << 23) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 // Scale-factor byte ID of both operands (bits 29-30 for A, 4-5 for B): which byte of each
-// 32-bit scale-factor column an MMA starts at.  With 32-element blocks an atom (4 bytes per
-// row) serves two 64-element MMAs: the first reads bytes 0-1 (ID 0), the second 2-3 (ID 2).
+// 32-bit scale-factor column an MMA starts at.  An atom holds 4 bytes per row: with
+// 32-element blocks it serves two 64-deep kind::mxf4nvf4 MMAs (IDs 0 and 2) or four 32-deep
+// kind::mxf8f6f4 MMAs (IDs 0..3); with 16-element blocks one MMA reads all 4 (ID 0).
 __host__ __device__ constexpr uint32_t idesc_with_sf_id(uint32_t idesc, uint32_t id) {
   return idesc | (id << 29) | (id << 4);
 }
-// Separate IDs for A (bits 29-30) and B (bits 4-5).
-__host__ __device__ constexpr uint32_t idesc_with_sf_ids(uint32_t idesc, uint32_t a_id,
-                                                         uint32_t b_id) {
-  return idesc | (a_id << 29) | (b_id << 4);
-}
-// The same byte ID also rides in bits 30-31 of the scale-factor TMEM address operand (the
-// lane field of these addresses is 0; CUTLASS's UMMA atoms pass it the same way).
+// The same ID is also put in bits 30-31 of the scale-factor TMEM address operands, the form
+// CUTLASS's UMMA atoms use (the lane field of these addresses is 0).  Measured on B200: the
+// MMA takes the ID from the descriptor; with the ID only in the address every MMA read byte 0.
 __host__ __device__ constexpr uint32_t sf_tmem_addr(uint32_t taddr, uint32_t id) {
   return taddr | (id << 30);
 }
