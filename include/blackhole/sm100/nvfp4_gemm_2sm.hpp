@@ -136,7 +136,7 @@ __device__ __forceinline__ void tile_coords_2sm(int tile, const Nvfp4Gemm2SmPara
 
 }  // namespace detail
 
-template <class KT>
+template <class KT, bool kGather = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
     nvfp4_gemm_2sm_kernel(const __grid_constant__ Nvfp4Gemm2SmParams p) {
 #if defined(BLACKHOLE_ARCH_SM100)
@@ -451,7 +451,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
           tma_store_2d(&p.tmap_d, box, col0 + 64 * u, row0, pol_d);
           bulk_commit_group();
         }
-        if (p.num_peers > 0) {
+        if constexpr (kGather) {
           // the same box to every further buffer: 8 lanes per 128-byte row segment
 #pragma unroll 1
           for (int it = 0; it < 8; ++it) {
@@ -472,7 +472,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
       stage_store(v2, v3, 1);
     }
     if (lane == 0) bulk_wait_group<0>();
-    if (p.num_peers > 0) __threadfence_system();
+    if constexpr (kGather) __threadfence_system();
     __syncwarp();
   }
 
@@ -492,7 +492,14 @@ template <class KT>
 inline cudaError_t launch_2sm(int M, int N, int K, const void* A, const void* SFA, const void* B,
                               const void* SFB, void* D, float alpha, DeviceState* st, int dev,
                               cudaStream_t stream, const GatherSpec* g = nullptr) {
-  cudaError_t e = set_smem_once(nvfp4_gemm_2sm_kernel<KT>, KT::SmemBytes, dev);
+  // gather mode has its own instantiation (NVFP4 only: the gather entry point's format), so
+  // the plain GEMM carries none of its code
+  constexpr bool kCanGather = std::is_same_v<typename KT::Fmt, Nvfp4Format>;
+  if (g && !kCanGather) return cudaErrorInvalidValue;
+  auto* kernel = nvfp4_gemm_2sm_kernel<KT, false>;
+  if constexpr (kCanGather)
+    if (g) kernel = nvfp4_gemm_2sm_kernel<KT, true>;
+  cudaError_t e = set_smem_once(kernel, KT::SmemBytes, dev);
   if (e != cudaSuccess) return e;
   Nvfp4Gemm2SmParams p;
   e = make_a_tmap<typename KT::Fmt>(&p.tmap_a, A, M, K, KT::CtaM);
@@ -544,7 +551,7 @@ inline cudaError_t launch_2sm(int M, int N, int K, const void* A, const void* SF
       cfg.blockDim = dim3(KT::NumThreads, 1, 1);
       cfg.dynamicSmemBytes = KT::SmemBytes;
       int n = 0;
-      e = cudaOccupancyMaxActiveClusters(&n, nvfp4_gemm_2sm_kernel<KT>, &cfg);
+      e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
       if (e != cudaSuccess || n <= 0) {
         cudaGetLastError();
         n = st->num_sms / 2;
@@ -554,7 +561,7 @@ inline cudaError_t launch_2sm(int M, int N, int K, const void* A, const void* SF
     clusters = resident[dev & 63];
   }
   if (p.num_tiles < clusters) clusters = p.num_tiles;
-  e = launch_pdl(nvfp4_gemm_2sm_kernel<KT>, dim3(2 * clusters), dim3(KT::NumThreads), KT::SmemBytes,
+  e = launch_pdl(kernel, dim3(2 * clusters), dim3(KT::NumThreads), KT::SmemBytes,
                  stream, p);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();

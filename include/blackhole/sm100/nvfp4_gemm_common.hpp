@@ -5,6 +5,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <type_traits>
 
 #include <cuda_runtime_api.h>
 

@@ -194,7 +194,7 @@ __device__ __forceinline__ void st_release(uint32_t* p, uint32_t v) {
 
 }  // namespace skinny_detail
 
-template <class KT>
+template <class KT, bool kGather = false>
 __global__ void __launch_bounds__(KT::NumThreads, 1)
     nvfp4_gemm_skinny_kernel(const __grid_constant__ Nvfp4SkinnyParams p) {
 #if defined(BLACKHOLE_ARCH_SM100)
@@ -516,13 +516,16 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
         if (m0 + m < p.M && n < p.N) {
           __nv_bfloat16 b = __float2bfloat16_rn(a * v[m]);
           const uint16_t bits = *reinterpret_cast<uint16_t*>(&b);
-          const int64_t off = int64_t(m0 + m) * p.ldd + n;
+          // the plain GEMM keeps D's own row stride; gather mode (its own instantiation, so
+          // the plain one carries none of its code) also stores to every further buffer
+          const int64_t off = int64_t(m0 + m) * (kGather ? p.ldd : int64_t(p.N)) + n;
           p.d[off] = bits;
-          for (int q = 0; q < p.num_peers; ++q) p.peer_d[q][off] = bits;
+          if constexpr (kGather)
+            for (int q = 0; q < p.num_peers; ++q) p.peer_d[q][off] = bits;
         }
       }
     }
-    if (p.num_peers > 0) __threadfence_system();
+    if constexpr (kGather) __threadfence_system();
   }
 
   tc_fence_before();
@@ -545,7 +548,13 @@ inline cudaError_t launch_skinny(int M, int N, int K, const void* A, const void*
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  e = set_smem_once(nvfp4_gemm_skinny_kernel<KT>, KT::SmemBytes, dev);
+  // gather mode has its own instantiation (NVFP4 only: the gather entry point's format)
+  constexpr bool kCanGather = std::is_same_v<typename KT::Fmt, Nvfp4Format>;
+  if (g && !kCanGather) return cudaErrorInvalidValue;
+  auto* kernel = nvfp4_gemm_skinny_kernel<KT, false>;
+  if constexpr (kCanGather)
+    if (g) kernel = nvfp4_gemm_skinny_kernel<KT, true>;
+  e = set_smem_once(kernel, KT::SmemBytes, dev);
   if (e != cudaSuccess) return e;
   Nvfp4SkinnyParams p;
   e = make_b_tmap<typename KT::Fmt>(&p.tmap_w, B, N, K, 128);
@@ -592,7 +601,7 @@ inline cudaError_t launch_skinny(int M, int N, int K, const void* A, const void*
                : 0;
   p.sf_k_atoms = static_cast<int>(sf_k_atoms_vs(K, KT::SFVecSize));
   p.l2_pf = prefetch ? l2_prefetch_ktiles : 0;
-  e = launch_pdl(nvfp4_gemm_skinny_kernel<KT>, dim3(grid), dim3(KT::NumThreads), KT::SmemBytes,
+  e = launch_pdl(kernel, dim3(grid), dim3(KT::NumThreads), KT::SmemBytes,
                  stream, p);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
