@@ -13,7 +13,8 @@ sets whose total size exceeds the 126 MB L2 (4 x 72 MB), so no step finds its in
 `value` = whole-job TFLOP/s from CUDA events around the K timed steps (max over ranks).
 A second figure times single launches after a 256 MB L2-flush write ("per_launch_l2_flush").
 `e2e` is the same GEMM through the C ABI with pinned host buffers: H2D of A/SFA/B/SFB and D2H
-of D inside the timed region.  The decode shape (configs[2], M=16 N=28672 K=8192) is
+of D of every step inside the timed region, the steps pipelined over upload / compute /
+download streams.  The decode shape (configs[2], M=16 N=28672 K=8192) is
 reported under "decode" in HBM GB/s, back to back over 3 rotating weight sets (396 MB), with
 M = 1, 64, 128 under "decode.sweep_by_M".  "prefill" is configs[3] (M=16384 N=8192 K=28672,
 1% outlier activations) and "nsplit" configs[4] (M=32768, N=65536 split over the ranks,
@@ -258,35 +259,61 @@ def time_gemm_flushed(M, N, K, A, SFA, B, SFB, D, alpha, steps, flush, world):
 
 
 def run_e2e(M, N, K, A, SFA, B, SFB, alpha, steps, world):
-    """C-ABI call with pinned host buffers; H2D inputs and D2H output inside the region."""
+    """The C-ABI call with pinned host buffers, H2D of every step's inputs and D2H of every
+    step's result inside the timed region, pipelined the way a serving loop runs it: step
+    i+1's inputs upload (copy stream) while step i computes and step i-1's result downloads
+    (a second copy stream; PCIe is full duplex), over two device buffer sets ordered by
+    events.  A step costs about its slowest part instead of the sum of the three."""
     import torch
     import blackhole_b200 as bh
 
     dev = A.device
-    hA, hSFA, hB, hSFB = (t.cpu().pin_memory() for t in (A, SFA, B, SFB))
-    dA, dSFA, dB, dSFB = (torch.empty_like(t) for t in (A, SFA, B, SFB))
-    dD = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
-    hD = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
-    stream = torch.cuda.current_stream()
-    h2d = sum(t.numel() * t.element_size() for t in (hA, hSFA, hB, hSFB))
-    d2h = hD.numel() * hD.element_size()
+    hIn = [t.cpu().pin_memory() for t in (A, SFA, B, SFB)]
+    dIn = [[torch.empty_like(t) for t in (A, SFA, B, SFB)] for _ in range(2)]
+    dD = [torch.empty((M, N), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    hD = [torch.empty((M, N), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    s_cmp = torch.cuda.current_stream()
+    s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    in_done = [torch.cuda.Event() for _ in range(2)]
+    cmp_done = [torch.cuda.Event() for _ in range(2)]
+    out_done = [torch.cuda.Event() for _ in range(2)]
+    h2d = sum(t.numel() * t.element_size() for t in hIn)
+    d2h = hD[0].numel() * hD[0].element_size()
+    # every event starts recorded, so the first waits on each buffer pass at once
+    for b in range(2):
+        for ev in (in_done[b], cmp_done[b], out_done[b]):
+            ev.record(s_cmp)
 
-    def step():
-        dA.copy_(hA, non_blocking=True)
-        dSFA.copy_(hSFA, non_blocking=True)
-        dB.copy_(hB, non_blocking=True)
-        dSFB.copy_(hSFB, non_blocking=True)
-        bh.nvfp4_bf16_gemm(M, N, K, dA, dSFA, dB, dSFB, dD, alpha)
-        hD.copy_(dD, non_blocking=True)
+    def step(k):
+        b = k % 2
+        s_in.wait_event(cmp_done[b])              # the GEMM that last read dIn[b] is done
+        with torch.cuda.stream(s_in):
+            for d, h in zip(dIn[b], hIn):
+                d.copy_(h, non_blocking=True)
+        in_done[b].record(s_in)
+        s_cmp.wait_event(in_done[b])
+        s_cmp.wait_event(out_done[b])             # the download that last read dD[b] is done
+        bh.nvfp4_bf16_gemm(M, N, K, *dIn[b], dD[b], alpha, stream=s_cmp)
+        cmp_done[b].record(s_cmp)
+        s_out.wait_event(cmp_done[b])
+        with torch.cuda.stream(s_out):
+            hD[b].copy_(dD[b], non_blocking=True)
+        out_done[b].record(s_out)
 
-    step()
+    step(0)
+    step(1)
+    torch.cuda.synchronize()
     barrier(world)
     s = torch.cuda.Event(enable_timing=True)
     e = torch.cuda.Event(enable_timing=True)
-    s.record(stream)
-    for _ in range(steps):
-        step()
-    e.record(stream)
+    s.record(s_cmp)
+    s_in.wait_event(s)
+    s_out.wait_event(s)
+    for k in range(steps):
+        step(k)
+    s_cmp.wait_stream(s_in)
+    s_cmp.wait_stream(s_out)
+    e.record(s_cmp)
     barrier(world)
     ms = s.elapsed_time(e) / steps
     return ms, h2d, d2h
@@ -745,8 +772,9 @@ def main():
         result["e2e"] = {"value": flops_rank * world / (ems * 1e-3) / 1e12, "unit": "TFLOP/s",
                          "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                          "ms_per_step": ems, "steps": esteps,
-                         "path": "blackhole_sm100_nvfp4_bf16_gemm (C ABI) + pinned host copies"}
-        result["gpu_launches"] += esteps + 1
+                         "path": "blackhole_sm100_nvfp4_bf16_gemm (C ABI) + pinned host copies, "
+                                 "steps pipelined over upload / compute / download streams"}
+        result["gpu_launches"] += esteps
 
     result["clocks"] = clk.summary()
 
