@@ -418,6 +418,13 @@ def library_baseline(M, N, K, sets, steps, warmup, world):
             "steps": steps, "clocks": clk.summary()}
 
 
+# Decode legs warm up with ~0.1 s of decode launches: measured on B200, a decode timed right
+# after the power-capped GEMM legs with 20 warm-up launches ran at 30-33 us instead of its
+# steady 25 us (the clocks recover over tens of milliseconds), i.e. it timed the previous
+# leg's state, not the decode's.
+DECODE_WARMUP = 4000
+
+
 def run_decode(args, dev, rank, world, hbm_peak, peak_src, Ms=(16, 1, 64, 128)):
     """M x 28672 x 8192 decode GEMMs over 3 rotating weight sets (396 MB), back to
     back.  Returns the M=16 line plus a per-M sweep."""
@@ -437,7 +444,7 @@ def run_decode(args, dev, rank, world, hbm_peak, peak_src, Ms=(16, 1, 64, 128)):
             dsets.append((Ad, SFAd, Bd, SFBd, float(scAd[1].item()) * gB))
         Dd = torch.empty((Md, Nd), dtype=torch.bfloat16, device=dev)
         dsteps = max(30, args.steps)
-        dtot = time_gemm(Md, Nd, Kd, dsets, Dd, dsteps, args.warmup, world)
+        dtot = time_gemm(Md, Nd, Kd, dsets, Dd, dsteps, max(args.warmup, DECODE_WARMUP), world)
         dms = max_over_ranks(dtot / dsteps, world)
         nbytes = gemm_bytes(Md, Nd, Kd)
         gbs = nbytes / (dms * 1e-3) / 1e9
@@ -447,6 +454,7 @@ def run_decode(args, dev, rank, world, hbm_peak, peak_src, Ms=(16, 1, 64, 128)):
                 "peak": hbm_peak, "peak_source": peak_src,
                 "frac_of_spec_8tbs": gbs / SPEC_HBM_GBS, "steps": dsteps,
                 "l2": "3 rotating weight sets (396 MB > 126 MB L2), back to back",
+                "warmup_launches": max(args.warmup, DECODE_WARMUP),
                 "host_enqueue_us_per_launch": time_gemm.host_us_per_launch,
                 "traffic": profiled_traffic(f"gemm_{Md}x{Nd}x{Kd}")}
         if Md == 16:
@@ -497,7 +505,7 @@ def run_mx(args, dev, rank, world, fp4_peak, hbm_peak, fmt="mxfp4"):
              for i in range(3)]
     Dd = torch.empty((Md, Nd), dtype=torch.bfloat16, device=dev)
     dsteps = max(30, min(args.steps, 2000))
-    tot = time_gemm(Md, Nd, Kd, dsets, Dd, dsteps, max(3, args.warmup), world, fmt=fmt)
+    tot = time_gemm(Md, Nd, Kd, dsets, Dd, dsteps, max(args.warmup, DECODE_WARMUP), world, fmt=fmt)
     dms = max_over_ranks(tot / dsteps, world)
     a_bytes = Md * Kd if a8 else Md * Kd // 2   # MXFP8: one byte per element
     nbytes = a_bytes + Nd * Kd // 2 + (Md + Nd) * Kd // 32 + 2 * Md * Nd
