@@ -57,6 +57,8 @@ def parse():
                     help="main: only the 8192^3-class GEMM; decode: only the M=16 GEMM "
                          "(small runs for profiler captures; the JSON line then lacks the other)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--decode-warmup", type=int, default=4000,
+                    help="decode warm-up launches (~0.1 s at 4000; fewer for profiler captures)")
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the configs[3] prefill and configs[4] N-split legs")
     ap.add_argument("--no-cpu", action="store_true")
@@ -421,8 +423,7 @@ def library_baseline(M, N, K, sets, steps, warmup, world):
 # Decode legs warm up with ~0.1 s of decode launches: measured on B200, a decode timed right
 # after the power-capped GEMM legs with 20 warm-up launches ran at 30-33 us instead of its
 # steady 25 us (the clocks recover over tens of milliseconds), i.e. it timed the previous
-# leg's state, not the decode's.
-DECODE_WARMUP = 4000
+# leg's state, not the decode's.  (--decode-warmup, default 4000.)
 
 
 def run_decode(args, dev, rank, world, hbm_peak, peak_src, Ms=(16, 1, 64, 128)):
@@ -444,7 +445,7 @@ def run_decode(args, dev, rank, world, hbm_peak, peak_src, Ms=(16, 1, 64, 128)):
             dsets.append((Ad, SFAd, Bd, SFBd, float(scAd[1].item()) * gB))
         Dd = torch.empty((Md, Nd), dtype=torch.bfloat16, device=dev)
         dsteps = max(30, args.steps)
-        dtot = time_gemm(Md, Nd, Kd, dsets, Dd, dsteps, max(args.warmup, DECODE_WARMUP), world)
+        dtot = time_gemm(Md, Nd, Kd, dsets, Dd, dsteps, max(args.warmup, args.decode_warmup), world)
         dms = max_over_ranks(dtot / dsteps, world)
         nbytes = gemm_bytes(Md, Nd, Kd)
         gbs = nbytes / (dms * 1e-3) / 1e9
@@ -454,7 +455,7 @@ def run_decode(args, dev, rank, world, hbm_peak, peak_src, Ms=(16, 1, 64, 128)):
                 "peak": hbm_peak, "peak_source": peak_src,
                 "frac_of_spec_8tbs": gbs / SPEC_HBM_GBS, "steps": dsteps,
                 "l2": "3 rotating weight sets (396 MB > 126 MB L2), back to back",
-                "warmup_launches": max(args.warmup, DECODE_WARMUP),
+                "warmup_launches": max(args.warmup, args.decode_warmup),
                 "host_enqueue_us_per_launch": time_gemm.host_us_per_launch,
                 "traffic": profiled_traffic(f"gemm_{Md}x{Nd}x{Kd}")}
         if Md == 16:
@@ -505,7 +506,7 @@ def run_mx(args, dev, rank, world, fp4_peak, hbm_peak, fmt="mxfp4"):
              for i in range(3)]
     Dd = torch.empty((Md, Nd), dtype=torch.bfloat16, device=dev)
     dsteps = max(30, min(args.steps, 2000))
-    tot = time_gemm(Md, Nd, Kd, dsets, Dd, dsteps, max(args.warmup, DECODE_WARMUP), world, fmt=fmt)
+    tot = time_gemm(Md, Nd, Kd, dsets, Dd, dsteps, max(args.warmup, args.decode_warmup), world, fmt=fmt)
     dms = max_over_ranks(tot / dsteps, world)
     a_bytes = Md * Kd if a8 else Md * Kd // 2   # MXFP8: one byte per element
     nbytes = a_bytes + Nd * Kd // 2 + (Md + Nd) * Kd // 32 + 2 * Md * Nd
