@@ -586,7 +586,7 @@ def run_nsplit(args, dev, rank, world, fp4_peak):
         go = GatheredOutput(M, N, rank, world)
 
         def fused():
-            bh.nvfp4_bf16_gemm_gather(M, sh.rows, K, A, SFA, B, SFB, go.dst, sh.row0, N, alpha)
+            bh.nvfp4_bf16_gemm_gather(M, sh.rows, K, A, SFA, B, SFB, go.dst_c, sh.row0, N, alpha)
             go.barrier()
 
         for _ in range(2):
@@ -637,7 +637,7 @@ def run_decode_gather(dev, rank, world, steps=50):
         dist.all_gather_into_tensor(g, D)
 
     def fused_step():
-        bh.nvfp4_bf16_gemm_gather(M, sh.rows, K, A, SFA, B, SFB, go.dst, sh.row0, N, alpha)
+        bh.nvfp4_bf16_gemm_gather(M, sh.rows, K, A, SFA, B, SFB, go.dst_c, sh.row0, N, alpha)
         go.barrier()
 
     res = {}

@@ -19,7 +19,7 @@ __all__ = [
     "nvfp4_bf16_gemm_ex", "workspace_bytes", "SCHEDULES", "nvfp4_bf16_gemm_noalloc",
     "selftest_bounded_wait", "mxfp4_bf16_gemm", "mxfp4_sf_storage_bytes", "mxfp4_quantize",
     "quantize_tensor_mxfp4", "mxf8f4_bf16_gemm", "mxfp8_quantize", "quantize_tensor_mxfp8",
-    "nvfp4_bf16_gemm_gather", "ipc_get_handle", "ipc_open", "ipc_close",
+    "nvfp4_bf16_gemm_gather", "peer_barrier", "ipc_get_handle", "ipc_open", "ipc_close",
 ]
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -90,6 +90,8 @@ def load():
     L.blackhole_sm100_nvfp4_bf16_gemm_gather.restype = i32
     L.blackhole_sm100_nvfp4_bf16_gemm_gather.argtypes = [i32, i32, i32, vp, vp, vp, vp, vp, i32, i64,
                                                          i64, ctypes.c_float, vp]
+    L.blackhole_sm100_peer_barrier.restype = i32
+    L.blackhole_sm100_peer_barrier.argtypes = [vp, i32, i32, ctypes.c_uint64, ctypes.c_uint64, vp]
     L.blackhole_sm100_ipc_get_handle.restype = i32
     L.blackhole_sm100_ipc_get_handle.argtypes = [vp, vp, ctypes.POINTER(ctypes.c_int64)]
     L.blackhole_sm100_ipc_open.restype = i32
@@ -246,13 +248,29 @@ def nvfp4_bf16_gemm_gather(M: int, N: int, K: int, A, SFA, B, SFB, dst, col0: in
     `dst` (row-major BF16, rows `ldd` elements apart) from inside the kernel.  dst[0] must be
     this GPU's memory; the others may be other GPUs' buffers mapped with ipc_open.  The caller
     synchronises the ranks afterwards (nothing in the call waits for other GPUs)."""
-    ptrs = (ctypes.c_void_p * max(1, len(dst)))(*[_ptr(d) for d in dst])
+    ptrs = dst if isinstance(dst, ctypes.Array) else pointer_array(dst)
     rc = load().blackhole_sm100_nvfp4_bf16_gemm_gather(
         int(M), int(N), int(K), _ptr(A), _ptr(SFA), _ptr(B), _ptr(SFB),
         ctypes.cast(ptrs, ctypes.c_void_p) if dst else None, len(dst), int(col0), int(ldd),
         float(alpha), _stream(stream))
     if rc != 0:
         raise BlackholeError("blackhole_sm100_nvfp4_bf16_gemm_gather", rc)
+
+
+def pointer_array(bufs):
+    """A ctypes array of the buffers' device pointers (build once, pass to every call)."""
+    return (ctypes.c_void_p * max(1, len(bufs)))(*[_ptr(b) for b in bufs])
+
+
+def peer_barrier(flags, world: int, rank: int, epoch: int, limit_ns: int = 1_000_000_000,
+                 stream=None) -> None:
+    """Stream-ordered barrier of a gathered N-split (see blackhole_sm100_peer_barrier):
+    flags[q] is rank q's flag array as mapped here (a list, or a pointer_array)."""
+    ptrs = flags if isinstance(flags, ctypes.Array) else pointer_array(flags)
+    rc = load().blackhole_sm100_peer_barrier(ctypes.cast(ptrs, ctypes.c_void_p), int(world),
+                                             int(rank), int(epoch), int(limit_ns), _stream(stream))
+    if rc != 0:
+        raise BlackholeError("blackhole_sm100_peer_barrier", rc)
 
 
 def ipc_get_handle(buf):

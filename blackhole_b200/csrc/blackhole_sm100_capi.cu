@@ -7,6 +7,7 @@
 #include <blackhole/sm100/nvfp4_gemm.hpp>
 #include <blackhole/sm100/nvfp4_quant.hpp>
 #include <blackhole/sm100/bounded_wait_selftest.hpp>
+#include <blackhole/sm100/peer_barrier.hpp>
 
 #include <cstring>
 #include <map>
@@ -125,6 +126,12 @@ int blackhole_sm100_ipc_close(void* ptr) {
     g_ipc_open.erase(it);
   }
   return static_cast<int>(cudaIpcCloseMemHandle(base));
+}
+
+int blackhole_sm100_peer_barrier(void* const* flags, int world, int rank, uint64_t epoch,
+                                 uint64_t limit_ns, cudaStream_t stream) {
+  return static_cast<int>(
+      blackhole::sm100::peer_barrier(flags, world, rank, epoch, limit_ns, stream));
 }
 
 int blackhole_sm100_nvfp4_bf16_gemm_gather(int M, int N, int K, const void* A, const void* SFA,

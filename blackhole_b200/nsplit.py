@@ -86,45 +86,61 @@ def nsplit_gemm(M: int, N: int, K: int, A, SFA, B, SFB, alpha: float, rank: int,
 
 
 class GatheredOutput:
-    """A row-major M x N BF16 buffer on every rank, mapped into every other rank (CUDA IPC).
+    """A row-major M x N BF16 buffer on every rank, mapped into every other rank (CUDA IPC),
+    plus the ranks' barrier flags.
 
     Collective: every rank of `group` constructs it with the same M and N.  `dst` lists the
-    destinations of this rank's gather call: its own buffer first, then the peers' mappings.
+    destinations of this rank's gather call (its own buffer first, then the peers' mappings;
+    `dst_c` the same as a ready-made pointer array), `barrier()` is the stream-ordered flag
+    barrier that makes every rank's tiles visible to work after it.
     """
 
-    def __init__(self, M: int, N: int, rank: int, world: int, group=None):
+    def __init__(self, M: int, N: int, rank: int, world: int, group=None,
+                 barrier_limit_ns: int = 1_000_000_000):
         import torch
         import torch.distributed as dist
 
         import blackhole_b200 as bh
 
         self.M, self.N, self.rank, self.world = M, N, rank, world
-        self.out = torch.empty((M, N), dtype=torch.bfloat16, device=torch.cuda.current_device())
-        self._peers = []
-        handles = [None] * world
+        dev = torch.cuda.current_device()
+        self.out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+        self.flags = torch.zeros(world, dtype=torch.int64, device=dev)
+        self._mapped = []
+        out_ptrs = {rank: self.out.data_ptr()}
+        flag_ptrs = {rank: self.flags.data_ptr()}
         if world > 1:
-            dist.all_gather_object(handles, bh.ipc_get_handle(self.out), group=group)
+            handles = [None] * world
+            dist.all_gather_object(handles, (bh.ipc_get_handle(self.out),
+                                             bh.ipc_get_handle(self.flags)), group=group)
             for q in range(world):
                 if q != rank:
-                    self._peers.append(bh.ipc_open(*handles[q]))
-        self.dst = [self.out] + self._peers
-        self._flag = torch.zeros(1, dtype=torch.int32, device=self.out.device)
-        self.group = group
+                    out_ptrs[q] = bh.ipc_open(*handles[q][0])
+                    flag_ptrs[q] = bh.ipc_open(*handles[q][1])
+                    self._mapped += [out_ptrs[q], flag_ptrs[q]]
+        self.dst = [self.out] + [out_ptrs[q] for q in range(world) if q != rank]
+        self.dst_c = bh.pointer_array(self.dst)
+        self.flags_c = bh.pointer_array([flag_ptrs[q] for q in range(world)])
+        self.epoch = 0
+        self.limit_ns = barrier_limit_ns
 
-    def barrier(self):
-        """Stream-ordered: returns once every rank's GEMM before it (hence every write into any
-        rank's buffer) has completed, as seen from this rank's stream."""
-        if self.world > 1:
-            import torch.distributed as dist
-            dist.all_reduce(self._flag, group=self.group)
+    def barrier(self, stream=None):
+        """Stream-ordered: work after it on this rank's stream sees every rank's gather writes
+        issued before their barriers.  Every rank calls it once per step."""
+        import blackhole_b200 as bh
+
+        self.epoch += 1
+        bh.peer_barrier(self.flags_c, self.world, self.rank, self.epoch, self.limit_ns,
+                        stream=stream)
 
     def close(self):
         import blackhole_b200 as bh
 
-        for p in self._peers:
+        for p in self._mapped:
             bh.ipc_close(p)
-        self._peers = []
+        self._mapped = []
         self.dst = [self.out]
+        self.dst_c = bh.pointer_array(self.dst)
 
 
 def nsplit_gemm_gathered(M: int, N: int, K: int, A, SFA, B, SFB, alpha: float, rank: int,
@@ -137,7 +153,7 @@ def nsplit_gemm_gathered(M: int, N: int, K: int, A, SFA, B, SFB, alpha: float, r
         raise ValueError("GatheredOutput was made for another shape")
     s = shard(N, K, rank, world)
     b, sfb = shard_views(B, SFB, N, K, rank, world)
-    bh.nvfp4_bf16_gemm_gather(M, s.rows, K, A, SFA, b, sfb, out.dst, s.row0, N, alpha,
+    bh.nvfp4_bf16_gemm_gather(M, s.rows, K, A, SFA, b, sfb, out.dst_c, s.row0, N, alpha,
                               stream=stream)
-    out.barrier()
+    out.barrier(stream=stream)
     return out.out

@@ -472,7 +472,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
       stage_store(v2, v3, 1);
     }
     if (lane == 0) bulk_wait_group<0>();
-    if constexpr (kGather) __threadfence_system();
     __syncwarp();
   }
 

@@ -35,6 +35,7 @@ enum : uint32_t {
   kStatusLoadTimeout = 1u,
   kStatusMmaTimeout = 2u,
   kStatusEpilogueTimeout = 4u,
+  kStatusBarrierTimeout = 8u,     // peer_barrier: a peer's signal did not arrive in time
 };
 
 // Shape / alignment check shared by every schedule and the C ABI (host only, no CUDA calls).

@@ -525,7 +525,6 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
         }
       }
     }
-    if constexpr (kGather) __threadfence_system();
   }
 
   tc_fence_before();

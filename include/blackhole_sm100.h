@@ -15,7 +15,7 @@
 extern "C" {
 #endif
 
-#define BLACKHOLE_SM100_ABI_VERSION 4
+#define BLACKHOLE_SM100_ABI_VERSION 5
 
 #if defined(__GNUC__)
 #define BLACKHOLE_SM100_API __attribute__((visibility("default")))
@@ -131,6 +131,19 @@ BLACKHOLE_SM100_API int blackhole_sm100_ipc_get_handle(const void* ptr, void* ha
                                                        int64_t* offset);
 BLACKHOLE_SM100_API int blackhole_sm100_ipc_open(const void* handle, int64_t offset, void** ptr);
 BLACKHOLE_SM100_API int blackhole_sm100_ipc_close(void* ptr);
+
+/* Stream-ordered barrier across the ranks of a gathered N-split (no counterpart in the
+ * reference, whose gather is NCCL's).  flags[q] is rank q's array of `world` 64-bit words
+ * (zero before the first call, 8-byte aligned) as mapped in this process, flags[rank] this
+ * GPU's own; epoch is 1 on the first call and one more on each later call.  Stores epoch with
+ * a system-scope release into this rank's word of every peer's array after everything earlier
+ * on `stream`, then waits until every peer's word in this GPU's array has reached epoch, so
+ * work after it on `stream` sees every rank's gathered tiles.  The wait is bounded by limit_ns
+ * (0 < limit_ns <= 1e10): on timeout it sets status bit 8 (blackhole_sm100_device_status) and
+ * returns.  1 <= world <= 8; one call per GPU per step (the ranks wait on one another). */
+BLACKHOLE_SM100_API int blackhole_sm100_peer_barrier(void* const* flags, int world, int rank,
+                                                     uint64_t epoch, uint64_t limit_ns,
+                                                     cudaStream_t stream);
 
 /* Self-test of the bounded-wait protocol (no counterpart in the reference): one CTA whose
  * "producer" warp waits limit_ns on a barrier nothing arrives on, gives up, raises the CTA

@@ -34,7 +34,7 @@ def test_library_exports_every_declared_symbol():
     L = bh.load()
     for s in syms:
         assert hasattr(L, s)
-    assert L.blackhole_sm100_abi_version() == 4
+    assert L.blackhole_sm100_abi_version() == 5
     assert "blackhole_sm100_mxfp4_bf16_gemm_ex" in syms and "blackhole_sm100_mxfp4_quantize" in syms
 
 
@@ -119,3 +119,21 @@ def test_mxf8f4_b_needs_32_byte_alignment():
     with pytest.raises(bh.BlackholeError) as ei:
         bh.mxf8f4_bf16_gemm(128, 128, 256, 4096, 4096, 4096 + 16, 4096, 4096, 1.0, stream=0)
     assert ei.value.code == 1
+
+
+@pytest.mark.parametrize("world,rank,epoch,limit", [(0, 0, 1, 10**9), (9, 0, 1, 10**9), (2, 2, 1, 10**9),
+                                                    (2, -1, 1, 10**9), (2, 0, 0, 10**9), (2, 0, 1, 0),
+                                                    (2, 0, 1, 2 * 10**10)])
+def test_peer_barrier_bad_arguments_rejected(world, rank, epoch, limit):
+    good = 1 << 20
+    with pytest.raises(bh.BlackholeError) as ei:
+        bh.peer_barrier([good] * max(world, 1), world, rank, epoch, limit, stream=0)
+    assert ei.value.code == 1
+
+
+def test_peer_barrier_null_or_misaligned_flags_rejected():
+    good = 1 << 20
+    for flags in ([good, 0], [good, good + 4]):
+        with pytest.raises(bh.BlackholeError) as ei:
+            bh.peer_barrier(flags, 2, 0, 1, 10**9, stream=0)
+        assert ei.value.code == 1
