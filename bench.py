@@ -18,7 +18,8 @@ download streams.  The decode shape (configs[2], M=16 N=28672 K=8192) is
 reported under "decode" in HBM GB/s, back to back over 3 rotating weight sets (396 MB), with
 M = 1, 64, 128 under "decode.sweep_by_M".  "prefill" is configs[3] (M=16384 N=8192 K=28672,
 1% outlier activations) and "nsplit" configs[4] (M=32768, N=65536 split over the ranks,
-K=8192; strong scaling, with the NCCL all-gather timed separately when P > 1).
+K=8192; strong scaling; with --gather at P > 1 also the NCCL all-gather, the fused gather and
+the tensor-parallel decode leg).
 "library_baseline" times cuBLASLt's NVFP4 GEMM on the same 8192^3 operands, for comparison.
 
 --impl reference runs the reference's host GEMM (the CPU oracle's restatement of
@@ -62,7 +63,9 @@ def parse():
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the configs[3] prefill and configs[4] N-split legs")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--gather", action="store_true", help="also time the NCCL all-gather (P>1)")
+    ap.add_argument("--gather", action="store_true",
+                    help="P > 1: also time the gathers (NCCL all-gather, the fused gather, and "
+                         "the tensor-parallel decode leg)")
     ap.add_argument("--no-library", action="store_true",
                     help="skip the cuBLASLt NVFP4 comparison leg (torch._scaled_mm, same operands)")
     ap.add_argument("--schedule", default="auto", choices=["auto", "1sm", "2sm"],
@@ -562,7 +565,7 @@ def run_nsplit(args, dev, rank, world, fp4_peak):
            "unit": "TFLOP/s", "scaling": "strong", "n_gpus": world,
            "ms_per_step": ms, "value": flops / (ms * 1e-3) / 1e12,
            "roofline_frac": flops / world / (ms * 1e-3) / 1e12 / fp4_peak, "steps": steps}
-    if world > 1:
+    if world > 1 and args.gather:
         g = torch.empty((world, M, sh.rows), dtype=torch.bfloat16, device=dev)
         dist.all_gather_into_tensor(g, D)
         barrier(world)
@@ -607,7 +610,7 @@ def run_nsplit(args, dev, rank, world, fp4_peak):
         go.close()
         del go
     del A, SFA, B, SFB, D
-    if world > 1:
+    if world > 1 and args.gather:
         out["decode_gather"] = run_decode_gather(dev, rank, world)
         out["steps"] += out["decode_gather"]["steps"]
     return out
@@ -658,7 +661,7 @@ def run_decode_gather(dev, rank, world, steps=50):
             "us_per_step_gemm_then_nccl": res["gemm_then_nccl"], "us_per_step_fused": res["fused"],
             "speedup": res["gemm_then_nccl"] / res["fused"], "steps": 2 * steps,
             "note": "each step includes its cross-GPU synchronisation (the all-gather, or the "
-                    "fused path's one-element all-reduce)"}
+                    "fused path's flag barrier)"}
 
 
 # ---------------------------------------------------------------------------------------
