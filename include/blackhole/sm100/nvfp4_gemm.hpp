@@ -15,12 +15,16 @@
 // (include/blackhole/sm120/nvfp4_gemm.hpp:588-637), plus an alpha (global scale) overload.
 //
 // Schedules (chosen by shape):
-//   * M <= 128 : skinny schedule (nvfp4_gemm_skinny.hpp) -- swap-AB, stream-K over all SMs,
+//   * M <= 16 : skinny schedule (nvfp4_gemm_skinny.hpp) -- swap-AB, stream-K over all SMs,
 //                HBM-bound; needs a small FP32 workspace (allocated here per device and
 //                stream on first use, or passed by the caller: nvfp4_bf16_gemm_ex).  It warms
 //                L2 with its first B / SFB tiles while the previous kernel in the stream is
 //                finishing (a prefetch only: results are those of plain stream order);
-//   * 128 < M <= 256 : one-SM schedule (nvfp4_gemm_1sm.hpp) -- 128 x 256 tiles;
+//   * 16 < M <= 256 : one-SM schedule (nvfp4_gemm_1sm.hpp) -- 128 x 256 tiles.  Measured on
+//                B200 (K = 1024..16384, N = 2048..28672): faster than the skinny schedule in
+//                every case but one from M = 32 up (M = 128, N = 28672, K = 8192: 30.5 vs
+//                38.3 us; M = 128, N = 4096, K = 4096: 10.8 vs 31.9 us), slower at M = 16
+//                (25.2 vs 30.9 us at N = 28672);
 //   * M > 256  : two-SM schedule (nvfp4_gemm_2sm.hpp) -- 256 x 256 tiles per CTA pair
 //                (cta_group::2): a third less operand traffic into each SM than the one-SM
 //                tile, which on B200 is what limits the tensor pipe once the kernel is power
@@ -112,7 +116,7 @@ inline cudaError_t block_scaled_bf16_gemm_ex(int M, int N, int K, void const* A,
   e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (schedule == Nvfp4Schedule::kAuto)
-    schedule = M <= 128   ? Nvfp4Schedule::kSkinny
+    schedule = M <= 16    ? Nvfp4Schedule::kSkinny
                : M <= 256 ? Nvfp4Schedule::kOneSm
                           : Nvfp4Schedule::kTwoSm;
   switch (schedule) {

@@ -41,8 +41,9 @@ extern "C" {
  * Pointers must be 16-byte aligned.  Errors: cudaErrorInvalidValue for a bad shape,
  * null or misaligned pointer; otherwise the launch status, as in nvfp4_gemm.hpp:594-636.
  * Stream-ordered.  The kernels are launched as programmatic dependents of the previous kernel
- * in the stream: they set up while it finishes, and for M <= 128 also prefetch their first B /
- * SFB tiles into L2 (a cache hint only), but read and write nothing before it completes. */
+ * in the stream: they set up while it finishes, and for M <= 16 also prefetch their first B /
+ * SFB tiles into L2 (a cache hint only), but read and write nothing before it completes.
+ * By shape: M <= 16 the skinny stream-K schedule, M <= 256 the one-SM, larger M the two-SM. */
 BLACKHOLE_SM100_API int blackhole_sm100_nvfp4_bf16_gemm(int M, int N, int K, const void* A, const void* SFA,
                                     const void* B, const void* SFB, void* D, float alpha,
                                     cudaStream_t stream);

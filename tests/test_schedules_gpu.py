@@ -30,7 +30,9 @@ def test_two_sm_schedule(M, N, K):
     _check(M, N, K, "2sm", seed=M + N + K)
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 256, 256), (300, 640, 512), (1024, 1024, 1024)])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 256), (300, 640, 512), (1024, 1024, 1024),
+                                   (17, 512, 1024), (33, 1000, 512), (64, 4096, 2048),
+                                   (100, 896, 4352), (48, 2048, 8192)])
 def test_one_sm_schedule(M, N, K):
     _check(M, N, K, "1sm", seed=M + 3 * N + K)
 
@@ -90,3 +92,17 @@ def test_k_tail(schedule, M, N, K):
     """K not a multiple of 256 (only K % 32 == 0): the last k-tile's A/B bytes past K and its
     scale-factor atoms past the last one read zeros."""
     _check(M, N, K, schedule, seed=3 * M + N + K)
+
+
+@pytest.mark.parametrize("M", [16, 17, 64, 128, 256, 257])
+def test_auto_schedule_matches_the_explicit_one(M):
+    """By shape: M <= 16 skinny, M <= 256 one-SM, larger two-SM; bit-identical to that schedule
+    forced explicitly."""
+    N, K = 1024, 2048
+    want = "skinny" if M <= 16 else ("1sm" if M <= 256 else "2sm")
+    A, SFA, B, SFB, alpha = C.make_operands(M, N, K, seed=M)
+    auto = C.run_gpu(M, N, K, A, SFA, B, SFB, alpha)
+    forced = C.run_gpu(M, N, K, A, SFA, B, SFB, alpha, schedule=want)
+    assert np.array_equal(auto, forced)
+    (bad, _, _, _), _ = C.check_full(M, N, K, A, SFA, B, SFB, alpha, auto)
+    assert bad == 0
