@@ -89,7 +89,6 @@ struct Nvfp4Gemm2SmTraitsT {
   // scale-factor buffer full/empty and the copy warp's drain barrier
   static constexpr int BarrierBytes = 8 * (2 * Stages + 4) + 16 + 8 * (2 * SfBufs + 1);
   static constexpr int SmemBytes = Stages * StageBytes + StagingBytes + BarrierBytes + 1024;
-  static constexpr int RasterGroupM = 8;         // in 256-row tiles
 
   static_assert(SmemBytes <= arch_traits<Arch::kSm100>::max_smem_per_cta, "smem budget");
   static_assert(SfCol + SfBufs * SfStride <= TmemCols, "TMEM budget");
@@ -108,6 +107,7 @@ struct Nvfp4Gemm2SmParams {
   float alpha;
   int M, N, K;
   int tiles_m, tiles_n, num_tiles;
+  int raster_m;           // tiles walk raster_m 256-row blocks at a time, all N for each group
   int k_tiles;
   int sf_k_atoms;
   int sf_tail;            // K % 256 != 0: tmap_sfa / tmap_sfb are atom-granular (y = atom)
@@ -122,9 +122,27 @@ struct Nvfp4Gemm2SmParams {
 
 namespace detail {
 
+// Tile-rows per raster group: a group's rows of A (and SFA) stay in L2 while every column of B
+// streams past, so the larger the group the fewer times B is re-read from HBM -- as long as
+// the group's A fits the share of the 126 MB L2 given to it here (36 MiB), past which A itself
+// is evicted.  Measured on B200: 8192^3 (1.06 MB per tile-row) 245 / 241 / 240 us at groups
+// of 8 / 16 / 32; 16384 x 8192 x 28672 (3.8 MB per tile-row) 1.64-1.65 / 1.71 / 1.89 ms.
+inline int raster_group_2sm(int K, int tiles_m) {
+  const int64_t row_bytes = int64_t(256) * (K / 2 + K / 16);
+  int64_t g = (int64_t(36) << 20) / (row_bytes > 0 ? row_bytes : 1);
+  if (g > 32) g = 32;
+  if (g < 4) g = 4;
+  if (g > tiles_m) g = tiles_m;
+  if (g < 1) g = 1;
+  // the fewest groups of at most g rows, then equal groups: a last group of a single row would
+  // stream all of B again for one row (16384 x 8192 x 28672: 1.67 ms at 9 rows, 7 groups + 1)
+  const int64_t groups = (tiles_m + g - 1) / g;
+  return static_cast<int>((tiles_m + groups - 1) / groups);
+}
+
 __device__ __forceinline__ void tile_coords_2sm(int tile, const Nvfp4Gemm2SmParams& p, int& m_blk,
                                                 int& n_blk) {
-  constexpr int G = 8;  // raster group, in 256-row tiles
+  const int G = p.raster_m;  // raster group, in 256-row tiles
   const int group_tiles = G * p.tiles_n;
   const int group = tile / group_tiles;
   const int first_m = group * G;
@@ -534,6 +552,7 @@ inline cudaError_t launch_2sm(int M, int N, int K, const void* A, const void* SF
   p.tiles_m = (M + KT::TileM - 1) / KT::TileM;
   p.tiles_n = (N + KT::TileN - 1) / KT::TileN;
   p.num_tiles = p.tiles_m * p.tiles_n;
+  p.raster_m = detail::raster_group_2sm(K, p.tiles_m);
   p.k_tiles = (K + KT::TileK - 1) / KT::TileK;
   p.sf_k_atoms = static_cast<int>(sf_k_atoms_vs(K, KT::SFVecSize));
   // Persistent grid = the number of 2-CTA clusters that can be resident at once.  GPCs with
