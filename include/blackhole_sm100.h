@@ -116,7 +116,7 @@ BLACKHOLE_SM100_API int blackhole_sm100_nvfp4_bf16_gemm_noalloc(int M, int N, in
  * M the two-SM schedule.  1 <= ndst <= 8, col0 % 8 == 0,
  * ldd % 8 == 0, col0 + N <= ldd, all dst 16-byte aligned; shapes as blackhole_sm100_nvfp4_bf16_gemm.
  * Asynchronous on `stream`; nothing orders it against other GPUs: the caller synchronises the
- * ranks after the call (e.g. a one-element NCCL all-reduce on the same stream) before any rank
+ * ranks after the call (e.g. blackhole_sm100_peer_barrier on the same stream) before any rank
  * reads its buffer, and before a call overwrites a buffer another rank may still read. */
 BLACKHOLE_SM100_API int blackhole_sm100_nvfp4_bf16_gemm_gather(int M, int N, int K, const void* A,
                                                                const void* SFA, const void* B,
