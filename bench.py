@@ -22,6 +22,9 @@ K=8192; strong scaling; with --gather at P > 1 also the NCCL all-gather, the fus
 the tensor-parallel decode leg).
 "library_baseline" times cuBLASLt's NVFP4 GEMM on the same 8192^3 operands, for comparison.
 
+The CPU leg ("cpu_baseline") times the host reference loop and, as the checker, compares its
+output with the first 128 rows of the bench's own 8192^3 GPU result ("parity_vs_gpu").
+
 --impl reference runs the reference's host GEMM (the CPU oracle's restatement of
 example/nvfp4_bf16_gemm.cu:161-168) on the host cores instead.
 """
@@ -335,7 +338,24 @@ def cpu_reference_rows(A, SFA, B, SFB, N, K, rows, threads, alpha):
     return time.perf_counter() - t0
 
 
-def cpu_baseline(A, SFA, B, SFB, N, K, alpha, M, budget_s=12.0):
+def cpu_parity(A, SFA, B, SFB, N, K, alpha, gpu_rows, threads):
+    """The checker half of the CPU leg: the host reference on the first rows of the timed
+    workload (untimed, with the per-element sum |a*b| the tolerance needs) against the bench's
+    own GPU output for the same operands.  Tolerance per element: one BF16 ulp of the larger
+    magnitude + |alpha| * K * 2^-24 * sum_k |a_k b_k| (FP32 reassociation)."""
+    import numpy as np
+    from oracle import oracle as O
+    rows = gpu_rows.shape[0]
+    ref, absdot = O.gemm_full(rows, N, K, A, SFA, B, SFB, alpha=alpha, nthreads=threads)
+    bad, maxerr, ratio, rel = O.check(ref, gpu_rows, alpha, K, absdot)
+    return {"rows": rows, "elements": rows * N, "mismatches": bad,
+            "bit_identical_frac": float(np.mean(ref.ravel() == gpu_rows.ravel())),
+            "max_abs_err": maxerr, "max_err_over_tol": ratio, "reference_rel_max": rel,
+            "tolerance": "ulp_bf16 + |alpha|*K*2^-24*sum|a*b| per element; reference_rel_max "
+                         "is the example's own |got-ref|/(|ref|+1e-3) (it accepts <= 0.05)"}
+
+
+def cpu_baseline(A, SFA, B, SFB, N, K, alpha, M, budget_s=12.0, gpu_rows=None):
     threads = os.cpu_count() or 1
     # calibrate on the full width, then size the sample (whole output rows) to the budget
     t = cpu_reference_rows(A, SFA, B, SFB, N, K, threads, threads, alpha)
@@ -343,10 +363,13 @@ def cpu_baseline(A, SFA, B, SFB, N, K, alpha, M, budget_s=12.0):
     rows = max(threads, min(M, int(budget_s / per_row) // threads * threads))
     t = cpu_reference_rows(A, SFA, B, SFB, N, K, rows, threads, alpha)
     tflops = 2.0 * rows * N * K / t / 1e12
-    return {"value": tflops, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-            "sample": f"{rows} full output rows x N={N} x K={K} of the host reference loop "
-                      f"(sequential FP32 dot, example/nvfp4_bf16_gemm.cu:161-168), "
-                      f"{threads} threads, {t:.1f} s; TFLOP/s = 2*rows*N*K/t"}
+    out = {"value": tflops, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+           "sample": f"{rows} full output rows x N={N} x K={K} of the host reference loop "
+                     f"(sequential FP32 dot, example/nvfp4_bf16_gemm.cu:161-168), "
+                     f"{threads} threads, {t:.1f} s; TFLOP/s = 2*rows*N*K/t"}
+    if gpu_rows is not None:
+        out["parity_vs_gpu"] = cpu_parity(A, SFA, B, SFB, N, K, alpha, gpu_rows, threads)
+    return out
 
 
 def reference_arm(args, world, rank):
@@ -715,6 +738,8 @@ def main():
     fsteps = min(args.steps, 20)
     ftimes = time_gemm_flushed(M, N, K, A, SFA, B, SFB, D, alpha, fsteps, flush, world)
     assert bh.device_status(torch.cuda.current_device()) == 0
+    # D now holds the GEMM of input set 0: its first 128 rows go to the CPU leg's parity check
+    check_rows = D[:min(M, 128)].view(torch.int16).cpu().numpy().view("uint16")
     total_ms = max_over_ranks(total_ms, world)
     ms_step = total_ms / args.steps
     flops_rank = 2.0 * M * N * K
@@ -804,7 +829,8 @@ def main():
         hSFA = SFA.cpu().numpy()
         hB = B.cpu().numpy().reshape(-1)
         hSFB = SFB.cpu().numpy()
-        result["cpu_baseline"] = cpu_baseline(hA, hSFA, hB, hSFB, N, K, alpha, M)
+        result["cpu_baseline"] = cpu_baseline(hA, hSFA, hB, hSFB, N, K, alpha, M,
+                                              gpu_rows=check_rows)
 
     if rank == 0:
         print(json.dumps(result), flush=True)
