@@ -45,23 +45,33 @@ struct Nvfp4SkinnyTraits {
   static constexpr int TileK = Fmt::TileK;      // elements per k-tile (128-byte smem rows)
   static constexpr int KSteps = Geo::KSteps;
   static constexpr int RowBytes = Geo::RowBytes;
-  static constexpr int WBytes = TileW * RowBytes;           // 16 KB
-  static constexpr int XBytes = MPAD * RowBytes;            // 2..16 KB
+  // k-tiles per work unit (and shared-memory stage): 2 where B is expanded (MXFP8 x MXFP4,
+  // 128-deep k-tiles), so that a unit streams the same 256 K of weights as the 4-bit kinds and
+  // the per-unit cost (barrier round trip, copy and commit issue) is paid half as often.
+  static constexpr int KPS = Fmt::BExpand ? 2 : 1;
+  static constexpr int UnitK = KPS * TileK;                 // K-elements per unit: 256
+  static constexpr int UnitSteps = KPS * KSteps;            // MMAs per unit
+  static constexpr int TileWBytes = TileW * RowBytes;       // one k-tile of B: 16 KB
+  static constexpr int TileXBytes = MPAD * RowBytes;        // one k-tile of A: 2..16 KB
+  static constexpr int WBytes = KPS * TileWBytes;
+  static constexpr int XBytes = KPS * TileXBytes;
   // scale-factor atoms per 128 rows and k-tile: 4 (NVFP4), 2 (MXFP4), 1 (MXFP8 x MXFP4)
   static constexpr int StepsPerAtom = Geo::StepsPerAtom;
   static constexpr int SfAtoms = Geo::SfAtoms;
-  static constexpr int SFBytes = SfAtoms * 512;             // 2 KB per operand (NVFP4)
+  static constexpr int UnitAtoms = KPS * SfAtoms;           // atoms per unit: 4, 2, 2
+  static constexpr int SFBytes = UnitAtoms * 512;           // 2 KB per operand (NVFP4)
   static constexpr int StageBytes = WBytes + XBytes + 2 * SFBytes;
   // global bytes a stage's loads complete (the expanded 4-bit B is half its smem size)
-  static constexpr int StageTx = TileW * Geo::BRowTx + MPAD * Geo::ARowTx + 2 * SFBytes;
+  static constexpr int StageTx = KPS * (TileW * Geo::BRowTx + MPAD * Geo::ARowTx) + 2 * SFBytes;
   // NVFP4 / MXFP4: depths tuned per width.  An expanded 4-bit B (MXFP8 x MXFP4) moves half
   // its shared-memory bytes per stage, so its ring takes every stage that fits (at most 12).
   static constexpr int FitStages =
       (arch_traits<Arch::kSm100>::max_smem_per_cta - 1024 - 8 * (2 * 12 + 5) - 16) / StageBytes;
   static constexpr int Stages = Fmt::BExpand ? (FitStages < 12 ? FitStages : 12)
                                              : ((MPAD <= 32) ? 9 : (MPAD == 64 ? 8 : 6));
-  // k-tiles of B prefetched into L2 before the dependency wait (beyond the smem stages)
-  static constexpr int L2PrefetchKTiles = 20;
+  // units of B prefetched into L2 before the dependency wait (beyond the smem stages): 20
+  // k-tiles' worth of weight rows in every format
+  static constexpr int L2PrefetchKTiles = 20 / KPS;
   // ranges by ticket: the first CTA to start gets (1 + s) x, the last (1 - s) x the mean
   // work, s = RangeSkew / 64
   static constexpr int RangeSkew = 6;
@@ -80,7 +90,7 @@ struct Nvfp4SkinnyTraits {
   static constexpr uint32_t TmemCols = 512;
   static constexpr uint32_t AccStride = 128;                // two accumulators: [0,128), [128,256)
   static constexpr uint32_t SfwCol = 256;                   // 4 columns per atom
-  static constexpr uint32_t SfxCol = 256 + 4 * SfAtoms;     // 4 columns per atom
+  static constexpr uint32_t SfxCol = 256 + 4 * UnitAtoms;   // 4 columns per atom
 
   static constexpr int BarrierBytes = 8 * (2 * Stages + 5) + 16;
   static constexpr int SmemBytes = Stages * StageBytes + BarrierBytes + 1024;
@@ -120,7 +130,7 @@ struct Nvfp4SkinnyParams {
   uint32_t* status;
   float alpha;
   int M, N, K;
-  int kt_per_rb;        // ceil(K / 256)
+  int kt_per_rb;        // units per 128-row block: ceil(K / 256)
   int64_t units;        // ceil(N/128) * ceil(K/256)
   int grid;
   int skew;             // range of ticket t shrinks linearly: density (1 + s - 2 s t / grid), s = skew/64
@@ -289,11 +299,15 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
           kta_end = sa.kt1;
         }
         const int kt = kta++;
-        tma_prefetch_l2_2d(&p.tmap_w, kt * KT::RowBytes, sa.rb * KT::TileW);
-        // only the atoms that exist (the last k-tile of a K tail has fewer)
-        const int atoms = min(KT::SfAtoms, p.sf_k_atoms - KT::SfAtoms * kt);
-        bulk_prefetch_l2(p.sfw + int64_t(sa.rb) * p.sf_k_atoms * 512 + int64_t(kt) * KT::SfAtoms * 512,
-                         uint32_t(atoms) * 512u);
+#pragma unroll
+        for (int h = 0; h < KT::KPS; ++h)   // (a K tail's last unit may end inside its first half)
+          if ((kt * KT::KPS + h) * KT::TileK < p.K)
+            tma_prefetch_l2_2d(&p.tmap_w, (kt * KT::KPS + h) * KT::RowBytes, sa.rb * KT::TileW);
+        // only the atoms that exist (the last unit of a K tail has fewer)
+        const int atoms = min(KT::UnitAtoms, p.sf_k_atoms - KT::UnitAtoms * kt);
+        if (atoms > 0)
+          bulk_prefetch_l2(p.sfw + int64_t(sa.rb) * p.sf_k_atoms * 512 + int64_t(kt) * KT::UnitAtoms * 512,
+                           uint32_t(atoms) * 512u);
       };
       for (int i = 0; i < p.l2_pf; ++i) prefetch_next();
       pdl_wait_prior_grid();
@@ -311,17 +325,24 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
             break;
           }
           const uint32_t fb = full_bar(stage);
-          const int64_t k_off = int64_t(kt) * KT::SfAtoms * 512;
+          const int64_t k_off = int64_t(kt) * KT::UnitAtoms * 512;
           mbar_arrive_expect_tx(fb, KT::StageTx);
-          // A (small, L2-resident) ahead of B in the copy engine's queue
-          tma_load_2d(st_x(stage), &p.tmap_x, fb, kt * KT::RowBytes, 0, pol_x);
+          // A (small, L2-resident) ahead of B in the copy engine's queue; a unit's k-tiles sit
+          // side by side in the stage (rows past K read zeros)
+#pragma unroll
+          for (int h = 0; h < KT::KPS; ++h)
+            tma_load_2d(st_x(stage) + h * KT::TileXBytes, &p.tmap_x, fb,
+                        (kt * KT::KPS + h) * KT::RowBytes, 0, pol_x);
           if (p.sf_tail)  // atoms past K read zeros
-            tma_load_3d(st_sfx(stage), &p.tmap_sfx, fb, 0, KT::SfAtoms * kt, 0, pol_x);
+            tma_load_3d(st_sfx(stage), &p.tmap_sfx, fb, 0, KT::UnitAtoms * kt, 0, pol_x);
           else
             bulk_load(st_sfx(stage), p.sfx + k_off, KT::SFBytes, fb, pol_x);
-          tma_load_2d(st_w(stage), &p.tmap_w, fb, kt * KT::RowBytes, sg.rb * KT::TileW, pol_w);
+#pragma unroll
+          for (int h = 0; h < KT::KPS; ++h)
+            tma_load_2d(st_w(stage) + h * KT::TileWBytes, &p.tmap_w, fb,
+                        (kt * KT::KPS + h) * KT::RowBytes, sg.rb * KT::TileW, pol_w);
           if (p.sf_tail)
-            tma_load_3d(st_sfw(stage), &p.tmap_sfw, fb, 0, KT::SfAtoms * kt, sg.rb, pol_w);
+            tma_load_3d(st_sfw(stage), &p.tmap_sfw, fb, 0, KT::UnitAtoms * kt, sg.rb, pol_w);
           else
             bulk_load(st_sfw(stage), sfw_rb + k_off, KT::SFBytes, fb, pol_w);
           ++issued;
@@ -371,18 +392,20 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
         const uint32_t ready = more ? mbar_probe(full_bar(nstage), nphase) : 1u;
         {
 #pragma unroll
-          for (int j = 0; j < KT::SfAtoms; ++j) {
+          for (int j = 0; j < KT::UnitAtoms; ++j) {
             tc_cp_32x128b_warpx4_w(tmem + KT::SfwCol + 4 * j, desc_sf_atom(st_sfw(stage) + 512 * j));
             tc_cp_32x128b_warpx4_w(tmem + KT::SfxCol + 4 * j, desc_sf_atom(st_sfx(stage) + 512 * j));
           }
-          const uint64_t wdesc = desc_kmajor_sw128(st_w(stage));
-          const uint64_t xdesc = desc_kmajor_sw128(st_x(stage));
 #pragma unroll
-          for (int j = 0; j < KT::KSteps; ++j) {
+          for (int j = 0; j < KT::UnitSteps; ++j) {
+            // k-tile h of the unit, k-step jj inside its swizzled rows (+32 bytes per step)
+            const int h = j / KT::KSteps, jj = j % KT::KSteps;
+            const uint64_t wdesc = desc_kmajor_sw128(st_w(stage) + h * KT::TileWBytes);
+            const uint64_t xdesc = desc_kmajor_sw128(st_x(stage) + h * KT::TileXBytes);
             const int at = j / KT::StepsPerAtom;
             const uint32_t sid = KT::Geo::sf_id(j);   // byte in the entry
             tc_mma_bs_w<typename KT::Fmt>(
-                d_tmem, wdesc + 2 * j, xdesc + 2 * j, idesc_with_sf_id(idesc, sid),
+                d_tmem, wdesc + 2 * jj, xdesc + 2 * jj, idesc_with_sf_id(idesc, sid),
                 sf_tmem_addr(tmem + KT::SfwCol + 4 * at, sid),
                 sf_tmem_addr(tmem + KT::SfxCol + 4 * at, sid), (kt != sg.kt0 || j != 0) ? 1u : 0u);
           }
@@ -560,12 +583,12 @@ inline cudaError_t launch_skinny(int M, int N, int K, const void* A, const void*
   if (e != cudaSuccess) return e;
   e = make_a_tmap<typename KT::Fmt>(&p.tmap_x, A, M, K, KT::MPAD);
   if (e != cudaSuccess) return e;
-  p.kt_per_rb = (K + KT::TileK - 1) / KT::TileK;
-  p.sf_tail = K % KT::TileK != 0;
+  p.kt_per_rb = (K + KT::UnitK - 1) / KT::UnitK;
+  p.sf_tail = K % KT::UnitK != 0;
   if (p.sf_tail) {
-    e = make_sf_tmap_atoms(&p.tmap_sfw, SFB, N, K, 1, KT::SfAtoms, KT::SFVecSize);
+    e = make_sf_tmap_atoms(&p.tmap_sfw, SFB, N, K, 1, KT::UnitAtoms, KT::SFVecSize);
     if (e != cudaSuccess) return e;
-    e = make_sf_tmap_atoms(&p.tmap_sfx, SFA, M, K, 1, KT::SfAtoms, KT::SFVecSize);
+    e = make_sf_tmap_atoms(&p.tmap_sfx, SFA, M, K, 1, KT::UnitAtoms, KT::SFVecSize);
     if (e != cudaSuccess) return e;
   }
   p.units = int64_t((N + 127) / 128) * p.kt_per_rb;
