@@ -8,7 +8,8 @@
 // and the M activation rows become the UMMA N (padded to MPAD = 16/32/64/128; TMA
 // zero-fills rows >= M):
 //
-//   * work unit = (128-row block rb of B, 256-wide k-tile kt); U = ceil(N/128) * K/256 units are
+//   * work unit = (128-row block rb of B, K-slice kt of UnitK = 256 or 512 elements: one or two
+//     k-tiles of 128-byte shared-memory rows); U = ceil(N/128) * ceil(K/UnitK) units are
 //     split into equal contiguous ranges, one per persistent CTA (stream-K), so every SM
 //     streams the same number of bytes;
 //   * each CTA walks its range backwards in row-block segments; a segment accumulates in
@@ -46,10 +47,13 @@ struct Nvfp4SkinnyTraits {
   static constexpr int KSteps = Geo::KSteps;
   static constexpr int RowBytes = Geo::RowBytes;
   // k-tiles per work unit (and shared-memory stage): 2 where B is expanded (MXFP8 x MXFP4,
-  // 128-deep k-tiles), so that a unit streams the same 256 K of weights as the 4-bit kinds and
-  // the per-unit cost (barrier round trip, copy and commit issue) is paid half as often.
-  static constexpr int KPS = Fmt::BExpand ? 2 : 1;
-  static constexpr int UnitK = KPS * TileK;                 // K-elements per unit: 256
+  // 128-deep k-tiles) and at MPAD = 16 for every format, 1 otherwise.  The per-unit cost
+  // (barrier round trip, scale-factor copy and commit issue) is then paid once per 32 KB
+  // (4-bit) or 16 KB (expanded) of weights; measured on B200 at N = 28672, K = 8192: M = 16
+  // NVFP4 25.5 -> 23.7 us, MXFP4 24.1 -> 21.9 us, MXFP8 x MXFP4 39.0 -> 27.3 us.  Wider
+  // activation tiles (MPAD >= 32) keep one k-tile per stage, where the ring depth matters more.
+  static constexpr int KPS = (Fmt::BExpand || MPAD <= 16) ? 2 : 1;
+  static constexpr int UnitK = KPS * TileK;                 // K-elements per unit
   static constexpr int UnitSteps = KPS * KSteps;            // MMAs per unit
   static constexpr int TileWBytes = TileW * RowBytes;       // one k-tile of B: 16 KB
   static constexpr int TileXBytes = MPAD * RowBytes;        // one k-tile of A: 2..16 KB
@@ -58,7 +62,7 @@ struct Nvfp4SkinnyTraits {
   // scale-factor atoms per 128 rows and k-tile: 4 (NVFP4), 2 (MXFP4), 1 (MXFP8 x MXFP4)
   static constexpr int StepsPerAtom = Geo::StepsPerAtom;
   static constexpr int SfAtoms = Geo::SfAtoms;
-  static constexpr int UnitAtoms = KPS * SfAtoms;           // atoms per unit: 4, 2, 2
+  static constexpr int UnitAtoms = KPS * SfAtoms;           // scale-factor atoms per unit
   static constexpr int SFBytes = UnitAtoms * 512;           // 2 KB per operand (NVFP4)
   static constexpr int StageBytes = WBytes + XBytes + 2 * SFBytes;
   // global bytes a stage's loads complete (the expanded 4-bit B is half its smem size)
@@ -67,7 +71,7 @@ struct Nvfp4SkinnyTraits {
   // its shared-memory bytes per stage, so its ring takes every stage that fits (at most 12).
   static constexpr int FitStages =
       (arch_traits<Arch::kSm100>::max_smem_per_cta - 1024 - 8 * (2 * 12 + 5) - 16) / StageBytes;
-  static constexpr int Stages = Fmt::BExpand ? (FitStages < 12 ? FitStages : 12)
+  static constexpr int Stages = KPS == 2 ? (FitStages < 12 ? FitStages : 12)
                                              : ((MPAD <= 32) ? 9 : (MPAD == 64 ? 8 : 6));
   // units of B prefetched into L2 before the dependency wait (beyond the smem stages): 20
   // k-tiles' worth of weight rows in every format
@@ -130,8 +134,8 @@ struct Nvfp4SkinnyParams {
   uint32_t* status;
   float alpha;
   int M, N, K;
-  int kt_per_rb;        // units per 128-row block: ceil(K / 256)
-  int64_t units;        // ceil(N/128) * ceil(K/256)
+  int kt_per_rb;        // units per 128-row block: ceil(K / UnitK)
+  int64_t units;        // ceil(N/128) * ceil(K/UnitK)
   int grid;
   int skew;             // range of ticket t shrinks linearly: density (1 + s - 2 s t / grid), s = skew/64
   int sf_k_atoms;
