@@ -18,8 +18,9 @@ download streams.  The decode shape (configs[2], M=16 N=28672 K=8192) is
 reported under "decode" in HBM GB/s, back to back over 3 rotating weight sets (396 MB), with
 M = 1, 64, 128 under "decode.sweep_by_M".  "prefill" is configs[3] (M=16384 N=8192 K=28672,
 1% outlier activations) and "nsplit" configs[4] (M=32768, N=65536 split over the ranks,
-K=8192; strong scaling; with --gather at P > 1 also the NCCL all-gather, the fused gather and
-the tensor-parallel decode leg).
+K=8192; strong scaling; at P > 1 also, unless --no-gather, the NCCL all-gather, the fused
+gather with its NVLink figures and the tensor-parallel decode leg, each checked against the
+oracle on a sample).  "parity" holds every rank's check of its own timed output.
 "library_baseline" times cuBLASLt's NVFP4 GEMM on the same 8192^3 operands, for comparison.
 
 The CPU leg ("cpu_baseline") times the host reference loop and, as the checker, compares its
@@ -66,9 +67,9 @@ def parse():
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the configs[3] prefill and configs[4] N-split legs")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--gather", action="store_true",
-                    help="P > 1: also time the gathers (NCCL all-gather, the fused gather, and "
-                         "the tensor-parallel decode leg)")
+    ap.add_argument("--no-gather", action="store_true",
+                    help="P > 1: skip the gather legs (NCCL all-gather, the fused gather and the "
+                         "tensor-parallel decode leg), which run by default")
     ap.add_argument("--no-library", action="store_true",
                     help="skip the cuBLASLt NVFP4 comparison leg (torch._scaled_mm, same operands)")
     ap.add_argument("--schedule", default="auto", choices=["auto", "1sm", "2sm"],
@@ -100,7 +101,7 @@ class ClockSampler:
     REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
                "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, device_index, interval=0.005):
+    def __init__(self, device_index, interval=0.001):
         self.samples, self.reasons = [], set()
         self.max_mhz = None
         self._stop = threading.Event()
@@ -330,11 +331,23 @@ def run_e2e(M, N, K, A, SFA, B, SFB, alpha, steps, world):
 # ---------------------------------------------------------------------------------------
 # CPU legs (the oracle restatement of the reference's host loop)
 # ---------------------------------------------------------------------------------------
-def cpu_reference_rows(A, SFA, B, SFB, N, K, rows, threads, alpha):
-    """Reference host GEMM on `rows` full output rows (all N columns); returns seconds."""
+def decoded_operands(A, SFA, B, SFB, rows_a, rows_b, K):
+    """The float arrays the reference example builds before its host loop (element values
+    and per-16 scale values, example/nvfp4_bf16_gemm.cu:159-168 reads them as refA / sfaVal):
+    rows_a rows of A and rows_b rows of B.  Made once, outside any timed region."""
     from oracle import oracle as O
+    vA, sA = O.decode_operand(A[:rows_a * K // 2], SFA, rows_a, K)
+    vB, sB = O.decode_operand(B[:rows_b * K // 2], SFB, rows_b, K)
+    return vA, sA, vB, sB
+
+
+def cpu_loop_seconds(dec, rows, alpha, threads):
+    """The example's host loop (a = vA*sA, b = vB*sB, acc += a*b in k order, then
+    bf16(alpha*acc)) on `rows` full output rows against every decoded row of B; seconds."""
+    from oracle import oracle as O
+    vA, sA, vB, sB = dec
     t0 = time.perf_counter()
-    O.gemm_full(rows, N, K, A, SFA, B, SFB, alpha=alpha, nthreads=threads, want_absdot=False)
+    O.ref_loop(vA[:rows], sA[:rows], vB, sB, alpha, nthreads=threads)
     return time.perf_counter() - t0
 
 
@@ -342,30 +355,36 @@ def cpu_parity(A, SFA, B, SFB, N, K, alpha, gpu_rows, threads):
     """The checker half of the CPU leg: the host reference on the first rows of the timed
     workload (untimed, with the per-element sum |a*b| the tolerance needs) against the bench's
     own GPU output for the same operands.  Tolerance per element: one BF16 ulp of the larger
-    magnitude + |alpha| * K * 2^-24 * sum_k |a_k b_k| (FP32 reassociation)."""
-    import numpy as np
+    magnitude + |alpha| * sqrt(K) * 2^-24 * sum_k |a_k b_k| (FP32 reassociation), the one the
+    parity tests assert; the worst-case K * 2^-24 bound is reported beside it."""
     from oracle import oracle as O
     rows = gpu_rows.shape[0]
     ref, absdot = O.gemm_full(rows, N, K, A, SFA, B, SFB, alpha=alpha, nthreads=threads)
-    bad, maxerr, ratio, rel = O.check(ref, gpu_rows, alpha, K, absdot)
-    return {"rows": rows, "elements": rows * N, "mismatches": bad,
-            "bit_identical_frac": float(np.mean(ref.ravel() == gpu_rows.ravel())),
-            "max_abs_err": maxerr, "max_err_over_tol": ratio, "reference_rel_max": rel,
-            "tolerance": "ulp_bf16 + |alpha|*K*2^-24*sum|a*b| per element; reference_rel_max "
-                         "is the example's own |got-ref|/(|ref|+1e-3) (it accepts <= 0.05)"}
+    r = O.check_report(ref, gpu_rows, alpha, K, absdot)
+    r.update({"rows": rows,
+              "tolerance": "ulp_bf16 + |alpha|*sqrt(K)*2^-24*sum|a*b| per element (worst-case "
+                           "bound: K*2^-24); reference_rel_max is the example's own "
+                           "|got-ref|/(|ref|+1e-3) (it accepts <= 0.05)"})
+    return r
 
 
 def cpu_baseline(A, SFA, B, SFB, N, K, alpha, M, budget_s=12.0, gpu_rows=None):
+    from oracle import oracle as O
     threads = os.cpu_count() or 1
-    # calibrate on the full width, then size the sample (whole output rows) to the budget
-    t = cpu_reference_rows(A, SFA, B, SFB, N, K, threads, threads, alpha)
-    per_row = t / threads
-    rows = max(threads, min(M, int(budget_s / per_row) // threads * threads))
-    t = cpu_reference_rows(A, SFA, B, SFB, N, K, rows, threads, alpha)
+    cal = min(threads, M)
+    dec = decoded_operands(A, SFA, B, SFB, cal, N, K)
+    # calibrate on `cal` full rows, then size the sample (whole output rows) to the budget
+    t = cpu_loop_seconds(dec, cal, alpha, threads)
+    per_row = t / cal
+    rows = max(cal, min(M, int(budget_s / per_row) // threads * threads))
+    vA, sA = O.decode_operand(A[:rows * K // 2], SFA, rows, K)
+    dec = (vA, sA, dec[2], dec[3])
+    t = cpu_loop_seconds(dec, rows, alpha, threads)
     tflops = 2.0 * rows * N * K / t / 1e12
     out = {"value": tflops, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-           "sample": f"{rows} full output rows x N={N} x K={K} of the host reference loop "
-                     f"(sequential FP32 dot, example/nvfp4_bf16_gemm.cu:161-168), "
+           "sample": f"{rows} full output rows x N={N} x K={K} of the host reference loop in the "
+                     f"example's form (example/nvfp4_bf16_gemm.cu:159-168: a = vA*sA, "
+                     f"b = vB*sB, acc += a*b, values and scales decoded before the loop), "
                      f"{threads} threads, {t:.1f} s; TFLOP/s = 2*rows*N*K/t"}
     if gpu_rows is not None:
         out["parity_vs_gpu"] = cpu_parity(A, SFA, B, SFB, N, K, alpha, gpu_rows, threads)
@@ -373,7 +392,10 @@ def cpu_baseline(A, SFA, B, SFB, N, K, alpha, M, budget_s=12.0, gpu_rows=None):
 
 
 def reference_arm(args, world, rank):
-    """--impl reference: the reference's host GEMM on the host cores, rank 0 only."""
+    """--impl reference: the reference's host GEMM loop on the host cores, rank 0 only.  Each
+    step is the loop on 4 full output rows per thread (all N columns, all K): the same loop,
+    form and sample shape as this bench's cpu_baseline leg, with the operands decoded once
+    before the timed steps as the example does before its loop."""
     import numpy as np
     from oracle import oracle as O
 
@@ -381,29 +403,34 @@ def reference_arm(args, world, rank):
         return None
     M, N, K = args.m, args.n, args.k
     threads = os.cpu_count() or 1
-    # Inputs: the same recipe on the host (seeded), only the rows/columns a step touches.
-    cols = min(N, 2048)
-    xa = O.gen_normal(1, threads * K).reshape(threads, K)
-    xb = O.gen_normal(2, cols * K).reshape(cols, K)
+    # Inputs: the same recipe on the host (seeded): the rows a step touches.
+    xa = O.gen_normal(1, 4 * threads * K).reshape(4 * threads, K)
+    xb = O.gen_normal(2, N * K).reshape(N, K)
     A, SFA, ga = O.quantize(xa)
     B, SFB, gb = O.quantize(xb)
+    del xa, xb
     alpha = float(np.float32(ga) * np.float32(gb))
-    # per-step sample: `threads` rows x `cols` columns x K, sized so the run stays short
-    t_one = cpu_reference_rows(A, SFA, B, SFB, cols, K, threads, threads, alpha)
+    dec = decoded_operands(A, SFA, B, SFB, 4 * threads, N, K)
+    # per-step sample: 4 rows per thread x N columns x K (several rows per thread, as in the
+    # cpu_baseline leg's sample), fewer if the run would be long
+    rows = 4 * threads
+    t_one = cpu_loop_seconds(dec, rows, alpha, threads)
     total_steps = args.steps + args.warmup
-    budget = 90.0
+    budget = 150.0
     if t_one * total_steps > budget:
-        cols = max(128, int(cols * budget / (t_one * total_steps)) // 128 * 128)
+        rows = max(1, int(rows * budget / (t_one * total_steps)))
     for _ in range(args.warmup):
-        cpu_reference_rows(A, SFA, B, SFB, cols, K, threads, threads, alpha)
+        cpu_loop_seconds(dec, rows, alpha, threads)
     times = []
     for _ in range(args.steps):
-        times.append(cpu_reference_rows(A, SFA, B, SFB, cols, K, threads, threads, alpha))
+        times.append(cpu_loop_seconds(dec, rows, alpha, threads))
     t = sum(times)
-    flops = 2.0 * threads * cols * K * args.steps
+    flops = 2.0 * rows * N * K * args.steps
     v = flops / t / 1e12
-    sample = (f"{threads} output rows x {cols} columns x K={K} per step of the host reference "
-              f"loop (example/nvfp4_bf16_gemm.cu:161-168), {threads} threads")
+    sample = (f"{rows} full output rows x N={N} x K={K} per step of the host reference loop in "
+              f"the example's form (example/nvfp4_bf16_gemm.cu:159-168), {threads} threads; "
+              f"operands decoded once before the steps, as the example builds refA / sfaVal "
+              f"before its loop")
     return {
         "metric": "NVFP4 GEMM TFLOPS @8192^3 (% FP4 peak); M=16 decode GEMM HBM GB/s",
         "impl": "reference", "value": v, "unit": "TFLOP/s", "n_gpus": args.gpus,
@@ -567,9 +594,68 @@ def run_prefill(args, dev, rank, world, fp4_peak):
             "roofline_frac": tf / fp4_peak, "l2": "2 rotating input sets (~800 MB), back to back"}
 
 
+NVLINK_GBS = 770.0   # measured peer copy on this pool's B200s, GB/s per direction per GPU
+
+
+def all_gather_objects(obj, world):
+    if world == 1:
+        return [obj]
+    import torch.distributed as dist
+    out = [None] * world
+    dist.all_gather_object(out, obj)
+    return out
+
+
+def gathered_parity(M, N, K, A, SFA, B, SFB, alpha, rank, world, row0, buf, S=1024,
+                    own_slice=False):
+    """Checks S sampled elements of this rank's gathered row-major M x N buffer against the
+    oracle.  Every rank draws the same sample points; each computes the oracle at the points in
+    its own N-slice (the only slice of B it holds), the ranks exchange those values, and every
+    rank compares its buffer (tiles written by every rank) with the whole set.  With
+    own_slice=True, buf is this rank's M x N/P slice and only the points inside it are checked
+    (no exchange)."""
+    import numpy as np
+    import torch
+    from oracle import oracle as O
+
+    rows = B.shape[0] if B.dim() == 2 else B.numel() * 2 // K
+    rng = np.random.default_rng(77)
+    ms = rng.integers(0, M, S)
+    ns = rng.integers(0, N, S)
+    mine = np.nonzero((ns >= row0) & (ns < row0 + rows))[0]
+    hA, hSFA, hB, hSFB = (t.cpu().numpy().reshape(-1) for t in (A, SFA, B, SFB))
+    threads = max(1, (os.cpu_count() or 1) // world)
+    ref, ad = O.gemm_sampled(M, rows, K, hA, hSFA, hB, hSFB, ms[mine], ns[mine] - row0, alpha,
+                             nthreads=threads)
+    dev = buf.device
+    if own_slice:
+        tm = torch.from_numpy(ms[mine]).to(dev)
+        tn = torch.from_numpy(ns[mine] - row0).to(dev)
+        got = buf[tm, tn].view(torch.int16).cpu().numpy().view(np.uint16)
+        r = O.check_report(ref, got, alpha, K, ad)
+        r["sample"] = f"the points of {S} random elements of M x N that fall in each rank's slice"
+        return r
+    # each slice has its own alpha (its B was quantised with its own global scale)
+    parts = all_gather_objects((mine, ref, ad, alpha), world)
+    full_ref = np.zeros(S, dtype=np.uint16)
+    full_ad = np.zeros(S, dtype=np.float64)
+    full_alpha = np.zeros(S, dtype=np.float64)
+    for idx, r, a, al in parts:
+        full_ref[idx] = r
+        full_ad[idx] = a
+        full_alpha[idx] = al
+    got = buf[torch.from_numpy(ms).to(dev), torch.from_numpy(ns).to(dev)]
+    got = got.view(torch.int16).cpu().numpy().view(np.uint16)
+    r = O.check_report(full_ref, got, full_alpha, K, full_ad)
+    r["sample"] = f"{S} random elements of the whole gathered M x N buffer, on every rank"
+    return r
+
+
 def run_nsplit(args, dev, rank, world, fp4_peak):
     """M=32768, N=65536 split evenly over the P ranks, K=8192, seed 4; A replicated.
-    Strong scaling (the whole GEMM is fixed); with and without the NCCL all-gather of C."""
+    Strong scaling (the whole GEMM is fixed).  At P > 1 also (unless --no-gather) the NCCL
+    all-gather of the C slices after the GEMM, and the gather fused into the GEMM (every rank
+    ends with the row-major M x N result), each with its parity against the oracle."""
     import torch
     import torch.distributed as dist
     from blackhole_b200.nsplit import shard
@@ -588,7 +674,11 @@ def run_nsplit(args, dev, rank, world, fp4_peak):
            "unit": "TFLOP/s", "scaling": "strong", "n_gpus": world,
            "ms_per_step": ms, "value": flops / (ms * 1e-3) / 1e12,
            "roofline_frac": flops / world / (ms * 1e-3) / 1e12 / fp4_peak, "steps": steps}
-    if world > 1 and args.gather:
+    # parity of every rank's slice (the plain GEMM) at the same sample points as the gathered
+    # buffer below: the slice's own columns, checked on each rank
+    par = gathered_parity(M, N, K, A, SFA, B, SFB, alpha, rank, world, sh.row0, D, own_slice=True)
+    out["parity_slices"] = _merge_parity(all_gather_objects(par, world))
+    if world > 1 and not args.no_gather:
         g = torch.empty((world, M, sh.rows), dtype=torch.bfloat16, device=dev)
         dist.all_gather_into_tensor(g, D)
         barrier(world)
@@ -599,13 +689,16 @@ def run_nsplit(args, dev, rank, world, fp4_peak):
         e.record()
         barrier(world)
         gms = max_over_ranks(s.elapsed_time(e) / 3, world)
+        nbytes_in = (world - 1) * M * sh.rows * 2
         out["gather"] = {"ms_per_step": gms, "layout": "[P][M][N/P] bf16",
-                         "bytes_per_gpu_in": (world - 1) * M * sh.rows * 2,
+                         "bytes_per_gpu_in": nbytes_in,
+                         "nvlink_gbs_per_gpu": nbytes_in / (gms * 1e-3) / 1e9,
+                         "with_gather_ms_per_step": ms + gms,
                          "with_gather_tflops": flops / ((ms + gms) * 1e-3) / 1e12}
         del g
         # the gather fused into the GEMM: each rank's epilogue stores its tiles into every
-        # rank's row-major M x N buffer (CUDA IPC mappings) while it computes the next tiles;
-        # a one-element NCCL all-reduce per step is the completion barrier
+        # rank's row-major M x N buffer (CUDA IPC mappings, two buffers alternating by step)
+        # while it computes the next tiles; the flag barrier over NVLink ends each step
         import blackhole_b200 as bh
         from blackhole_b200.nsplit import GatheredOutput
 
@@ -625,25 +718,49 @@ def run_nsplit(args, dev, rank, world, fp4_peak):
         e.record()
         barrier(world)
         fms = max_over_ranks(s.elapsed_time(e) / steps, world)
-        out["fused_gather"] = {"ms_per_step": fms, "tflops": flops / (fms * 1e-3) / 1e12,
-                               "layout": "row-major M x N on every GPU",
-                               "nvlink_bytes_out_per_gpu": (world - 1) * M * sh.rows * 2,
-                               "speedup_vs_gemm_then_nccl": (ms + gms) / fms, "steps": steps}
-        out["steps"] += steps
+        assert bh.device_status(torch.cuda.current_device()) == 0
+        nbytes_out = (world - 1) * M * sh.rows * 2
+        t_link = nbytes_out / (NVLINK_GBS * 1e9) * 1e3
+        t_math = flops / world / (fp4_peak * 1e12) * 1e3
+        bound = max(t_link, t_math)
+        out["fused_gather"] = {
+            "ms_per_step": fms, "tflops": flops / (fms * 1e-3) / 1e12,
+            "layout": "row-major M x N on every GPU",
+            "nvlink_bytes_out_per_gpu": nbytes_out,
+            "nvlink_gbs_per_gpu": nbytes_out / (fms * 1e-3) / 1e9,
+            "roofline": {"bound_ms": bound, "limiter": "nvlink" if t_link > t_math else "tensor",
+                         "nvlink_ms_at_770_gbs": t_link, "tensor_ms_at_fp4_peak": t_math,
+                         "frac": bound / fms},
+            "speedup_vs_gemm_then_nccl": (ms + gms) / fms, "steps": steps,
+            "parity": _merge_parity(all_gather_objects(
+                gathered_parity(M, N, K, A, SFA, B, SFB, alpha, rank, world, sh.row0, go.out),
+                world))}
+        out["steps"] += steps + 2
         go.close()
         del go
     del A, SFA, B, SFB, D
-    if world > 1 and args.gather:
+    if world > 1 and not args.no_gather:
         out["decode_gather"] = run_decode_gather(dev, rank, world)
         out["steps"] += out["decode_gather"]["steps"]
     return out
 
 
+def _merge_parity(reports):
+    """One record from the ranks' parity reports."""
+    n = sum(r["elements"] for r in reports)
+    return {"elements": n, "mismatches": sum(r["mismatches"] for r in reports),
+            "bit_identical_frac": sum(r["bit_identical_frac"] * r["elements"] for r in reports) / max(n, 1),
+            "max_err_over_tol": max(r["max_err_over_tol"] for r in reports),
+            "max_err_over_worst_case_bound": max(r["max_err_over_worst_case_bound"] for r in reports),
+            "ranks": len(reports), "sample": reports[0].get("sample", "")}
+
+
 def run_decode_gather(dev, rank, world, steps=50):
     """Tensor-parallel decode: configs[2]'s M=16, K=8192 GEMM with the N=28672 weights split
     over the ranks and the output all-gathered, per step either GEMM + NCCL all-gather
-    ([P][M][N/P]) or the gather fused into the skinny GEMM + its one-element all-reduce
-    barrier (row-major M x N on every GPU)."""
+    ([P][M][N/P]) or the gather fused into the skinny GEMM + the flag barrier over NVLink that
+    ends each step (row-major M x N on every GPU, two buffers alternating by step so that a
+    step never writes the buffer a slower rank may still read)."""
     import torch
     import torch.distributed as dist
     import blackhole_b200 as bh
@@ -678,11 +795,15 @@ def run_decode_gather(dev, rank, world, steps=50):
         e.record()
         barrier(world)
         res[name] = max_over_ranks(s.elapsed_time(e) / steps, world) * 1e3
+    assert bh.device_status(torch.cuda.current_device()) == 0
+    parity = _merge_parity(all_gather_objects(
+        gathered_parity(M, N, K, A, SFA, B, SFB, alpha, rank, world, sh.row0, go.out), world))
     go.close()
     del A, SFA, B, SFB, D, g, go
     return {"workload": f"M={M} N={N} K={K}, N split over {world} GPUs, output all-gathered",
             "us_per_step_gemm_then_nccl": res["gemm_then_nccl"], "us_per_step_fused": res["fused"],
             "speedup": res["gemm_then_nccl"] / res["fused"], "steps": 2 * steps,
+            "parity": parity,
             "note": "each step includes its cross-GPU synchronisation (the all-gather, or the "
                     "fused path's flag barrier)"}
 
@@ -784,7 +905,7 @@ def main():
         result["mxf8f4"] = run_mx(args, dev, rank, world, fp4_peak, hbm_peak, "mxf8f4")
         result["gpu_launches"] += result["mxf8f4"]["steps"]
 
-    if world > 1 and args.gather:
+    if world > 1 and not args.no_gather:
         import torch.distributed as dist
         out = torch.empty((world, M, N), dtype=torch.bfloat16, device=dev)
         for _ in range(3):
@@ -797,8 +918,10 @@ def main():
         e.record()
         barrier(world)
         gms = max_over_ranks(s.elapsed_time(e) / 10, world)
+        nbytes_in = (world - 1) * M * N * 2
         result["gather"] = {"ms_per_step": gms, "layout": "[P][M][N/P] bf16",
-                            "bytes_per_gpu_in": (world - 1) * M * N * 2,
+                            "bytes_per_gpu_in": nbytes_in,
+                            "nvlink_gbs_per_gpu": nbytes_in / (gms * 1e-3) / 1e9,
                             "with_gather_tflops": flops_rank * world / ((ms_step + gms) * 1e-3) / 1e12}
         del out
 
@@ -810,7 +933,15 @@ def main():
                          "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                          "ms_per_step": ems, "steps": esteps,
                          "path": "blackhole_sm100_nvfp4_bf16_gemm (C ABI) + pinned host copies, "
-                                 "steps pipelined over upload / compute / download streams"}
+                                 "steps pipelined over upload / compute / download streams",
+                         # the ceiling: every step moves its inputs and its 134 MB result over
+                         # PCIe and through host memory, shared by all GPUs of the node
+                         "host_link": {"h2d_gbs_per_gpu": h2d / (ems * 1e-3) / 1e9,
+                                       "d2h_gbs_per_gpu": d2h / (ems * 1e-3) / 1e9,
+                                       "d2h_gbs_all_gpus": world * d2h / (ems * 1e-3) / 1e9,
+                                       "h2d_gbs_all_gpus": world * h2d / (ems * 1e-3) / 1e9,
+                                       "gemm_share_of_step": ms_step / ems,
+                                       "limiter": "host copies (PCIe / host memory), not the GEMM"}}
         result["gpu_launches"] += esteps
 
     result["clocks"] = clk.summary()
@@ -824,11 +955,24 @@ def main():
         except Exception as exc:  # an older torch without FP4 _scaled_mm
             result["library_baseline"] = {"unavailable": repr(exc)[:200]}
 
+    hA = A.cpu().numpy().reshape(-1)
+    hSFA = SFA.cpu().numpy()
+    hB = B.cpu().numpy().reshape(-1)
+    hSFB = SFB.cpu().numpy()
+    # every rank checks the first 16 full rows of its own timed output (input set 0) against
+    # the oracle; rank 0 reports each rank's record
+    threads = max(1, (os.cpu_count() or 1) // world)
+    par = cpu_parity(hA, hSFA, hB, hSFB, N, K, alpha, check_rows[:16], threads)
+    par["rank"] = rank
+    per_rank = all_gather_objects(par, world)
+    result["parity"] = dict(_merge_parity(per_rank),
+                            sample="first 16 full output rows of every rank's timed GEMM "
+                                   "(input set 0) against the host reference",
+                            per_rank=[{k: r[k] for k in ("rank", "elements", "mismatches",
+                                                         "bit_identical_frac", "max_err_over_tol")}
+                                      for r in per_rank])
+
     if rank == 0 and world == 1 and not args.no_cpu:
-        hA = A.cpu().numpy().reshape(-1)
-        hSFA = SFA.cpu().numpy()
-        hB = B.cpu().numpy().reshape(-1)
-        hSFB = SFB.cpu().numpy()
         result["cpu_baseline"] = cpu_baseline(hA, hSFA, hB, hSFB, N, K, alpha, M,
                                               gpu_rows=check_rows)
 

@@ -20,6 +20,7 @@ __all__ = [
     "selftest_bounded_wait", "mxfp4_bf16_gemm", "mxfp4_sf_storage_bytes", "mxfp4_quantize",
     "quantize_tensor_mxfp4", "mxf8f4_bf16_gemm", "mxfp8_quantize", "quantize_tensor_mxfp8",
     "nvfp4_bf16_gemm_gather", "peer_barrier", "ipc_get_handle", "ipc_open", "ipc_close",
+    "selftest_skinny_partial_wait",
 ]
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -85,6 +86,10 @@ def load():
     L.blackhole_sm100_device_status.argtypes = [i32, ctypes.POINTER(ctypes.c_uint), i32]
     L.blackhole_sm100_nvfp4_quantize.restype = i32
     L.blackhole_sm100_nvfp4_quantize.argtypes = [vp, i32, i32, i32, vp, vp, vp, vp]
+    L.blackhole_sm100_selftest_skinny_partial_wait.restype = i32
+    L.blackhole_sm100_selftest_skinny_partial_wait.argtypes = [i32, i32, i32, vp, vp, vp, vp, vp,
+                                                               ctypes.c_float, vp, i64,
+                                                               ctypes.c_uint64, vp]
     L.blackhole_sm100_selftest_bounded_wait.restype = i32
     L.blackhole_sm100_selftest_bounded_wait.argtypes = [ctypes.c_uint64, vp, vp]
     L.blackhole_sm100_nvfp4_bf16_gemm_gather.restype = i32
@@ -308,12 +313,26 @@ def nvfp4_bf16_gemm_noalloc(M: int, N: int, K: int, A, SFA, B, SFB, D, alpha: fl
     """The GEMM for M <= 16 without any device allocation, for callers that must not
     allocate at call time.  Its scratch lives in a fixed array inside the library (sized for
     M <= 16 on up to 160 SMs), shared by every call: calls that overlap on the GPU race.
-    The first call on a device resolves the array's address; make it before any capture."""
+    The first call on a device resolves the array's address; make it before any capture (a
+    lookup that fails is tried again by the next call)."""
     rc = load().blackhole_sm100_nvfp4_bf16_gemm_noalloc(
         int(M), int(N), int(K), _ptr(A), _ptr(SFA), _ptr(B), _ptr(SFB), _ptr(D), float(alpha),
         _stream(stream))
     if rc != 0:
         raise BlackholeError("blackhole_sm100_nvfp4_bf16_gemm_noalloc", rc)
+
+
+def selftest_skinny_partial_wait(M: int, N: int, K: int, A, SFA, B, SFB, D, alpha: float,
+                                 workspace, partial_wait_ns: int, stream=None) -> None:
+    """Test hook: the skinny schedule with the finishers' wait for partial sums bounded by
+    partial_wait_ns (a tiny bound makes them give up, status bit 2).  workspace: a device
+    buffer of at least workspace_bytes(M, N, K) bytes."""
+    nbytes = int(workspace.numel() * workspace.element_size()) if hasattr(workspace, "numel") else 1 << 40
+    rc = load().blackhole_sm100_selftest_skinny_partial_wait(
+        int(M), int(N), int(K), _ptr(A), _ptr(SFA), _ptr(B), _ptr(SFB), _ptr(D), float(alpha),
+        _ptr(workspace), nbytes, int(partial_wait_ns), _stream(stream))
+    if rc != 0:
+        raise BlackholeError("blackhole_sm100_selftest_skinny_partial_wait", rc)
 
 
 def workspace_bytes(M: int, N: int, K: int) -> int:

@@ -39,11 +39,12 @@ static_assert(kNoAllocScratchBytes == 1316096, "documented size of the scratch a
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 // The symbol above names a host-side stand-in, not a device address, so the kernel must be
-// given the address that cudaGetSymbolAddress returns for the current device.
+// given the address that cudaGetSymbolAddress returns for the current device.  Only a
+// successful lookup is kept: a first call that fails (for instance one made during a stream
+// capture) returns its error and the next call looks the address up again.
 struct NoAllocDevice {
-  std::once_flag once;
-  cudaError_t err = cudaSuccess;
-  void* scratch = nullptr;
+  std::mutex mu;
+  void* scratch = nullptr;   // non-null once looked up
 };
 
 cudaError_t noalloc_scratch(void** out) {
@@ -53,8 +54,13 @@ cudaError_t noalloc_scratch(void** out) {
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   NoAllocDevice& d = devs[dev];
-  std::call_once(d.once, [&]() { d.err = cudaGetSymbolAddress(&d.scratch, g_noalloc_scratch); });
-  if (d.err != cudaSuccess) return d.err;
+  std::lock_guard<std::mutex> lock(d.mu);
+  if (!d.scratch) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    d.scratch = p;
+  }
   *out = d.scratch;
   return cudaSuccess;
 }
@@ -272,6 +278,19 @@ int blackhole_sm100_nvfp4_bf16_gemm_noalloc(int M, int N, int K, const void* A, 
   return static_cast<int>(blackhole::sm100::nvfp4_bf16_gemm_skinny(
       M, N, K, A, SFA, B, SFB, D, alpha, scratch, static_cast<int64_t>(kNoAllocScratchBytes),
       stream));
+}
+
+int blackhole_sm100_selftest_skinny_partial_wait(int M, int N, int K, const void* A,
+                                                 const void* SFA, const void* B, const void* SFB,
+                                                 void* D, float alpha, void* workspace,
+                                                 int64_t workspace_bytes, uint64_t partial_wait_ns,
+                                                 cudaStream_t stream) {
+  if (partial_wait_ns == 0 || partial_wait_ns > blackhole::sm100::ptx::kWaitLimitNs || M > 128)
+    return static_cast<int>(cudaErrorInvalidValue);
+  return static_cast<int>(blackhole::sm100::block_scaled_bf16_gemm_skinny<
+                          blackhole::sm100::Nvfp4Format>(
+      M, N, K, A, SFA, B, SFB, D, alpha, workspace, workspace_bytes, stream, 1 << 30, true,
+      nullptr, partial_wait_ns));
 }
 
 int blackhole_sm100_selftest_bounded_wait(uint64_t limit_ns, uint64_t* result,

@@ -86,13 +86,24 @@ def nsplit_gemm(M: int, N: int, K: int, A, SFA, B, SFB, alpha: float, rank: int,
 
 
 class GatheredOutput:
-    """A row-major M x N BF16 buffer on every rank, mapped into every other rank (CUDA IPC),
-    plus the ranks' barrier flags.
+    """Two row-major M x N BF16 buffers on every rank, each mapped into every other rank
+    (CUDA IPC), plus the ranks' barrier flags.  Step s of a gathered N-split writes buffer
+    s % 2 on every rank.
 
-    Collective: every rank of `group` constructs it with the same M and N.  `dst` lists the
-    destinations of this rank's gather call (its own buffer first, then the peers' mappings;
-    `dst_c` the same as a ready-made pointer array), `barrier()` is the stream-ordered flag
-    barrier that makes every rank's tiles visible to work after it.
+    Collective: every rank of `group` constructs it with the same M and N.
+
+    Why two buffers: a step's gather kernels store into the OTHER ranks' buffers.  With one
+    buffer, a rank that passed step s's barrier could start step s+1 and overwrite a slower
+    rank's buffer while that rank still reads its step-s result.  With two, step s+1 writes the
+    buffer of step s-1, and a rank reaches step s+1 only after every rank arrived at step s's
+    barrier, which each rank does after the work it queued before step s on the same stream,
+    its reads of the step s-1 result included.
+
+    Rule for callers: read a step's result (`out`, or the tensor nsplit_gemm_gathered returns)
+    on the stream passed to the step, before enqueueing the step after next; a step's result
+    is overwritten two steps later.  `dst_c` is this step's destination list for the gather
+    call (own buffer first, then the peers' mappings), `barrier()` the stream-ordered flag
+    barrier that ends a step and makes every rank's tiles visible to work after it.
     """
 
     def __init__(self, M: int, N: int, rank: int, world: int, group=None,
@@ -104,34 +115,64 @@ class GatheredOutput:
 
         self.M, self.N, self.rank, self.world = M, N, rank, world
         dev = torch.cuda.current_device()
-        self.out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+        self.bufs = [torch.empty((M, N), dtype=torch.bfloat16, device=dev) for _ in range(2)]
         self.flags = torch.zeros(world, dtype=torch.int64, device=dev)
         self._mapped = []
-        out_ptrs = {rank: self.out.data_ptr()}
+        ptrs = [{rank: b.data_ptr()} for b in self.bufs]
         flag_ptrs = {rank: self.flags.data_ptr()}
         if world > 1:
             handles = [None] * world
-            dist.all_gather_object(handles, (bh.ipc_get_handle(self.out),
-                                             bh.ipc_get_handle(self.flags)), group=group)
+            mine = tuple(bh.ipc_get_handle(t) for t in (*self.bufs, self.flags))
+            dist.all_gather_object(handles, mine, group=group)
             for q in range(world):
                 if q != rank:
-                    out_ptrs[q] = bh.ipc_open(*handles[q][0])
-                    flag_ptrs[q] = bh.ipc_open(*handles[q][1])
-                    self._mapped += [out_ptrs[q], flag_ptrs[q]]
-        self.dst = [self.out] + [out_ptrs[q] for q in range(world) if q != rank]
-        self.dst_c = bh.pointer_array(self.dst)
+                    for i in range(2):
+                        ptrs[i][q] = bh.ipc_open(*handles[q][i])
+                        self._mapped.append(ptrs[i][q])
+                    flag_ptrs[q] = bh.ipc_open(*handles[q][2])
+                    self._mapped.append(flag_ptrs[q])
+        self._dst = [[self.bufs[i]] + [ptrs[i][q] for q in range(world) if q != rank]
+                     for i in range(2)]
+        self._dst_c = [bh.pointer_array(d) for d in self._dst]
         self.flags_c = bh.pointer_array([flag_ptrs[q] for q in range(world)])
-        self.epoch = 0
+        self.epoch = 0          # flag barriers issued so far (the barrier kernel's epoch)
+        self.steps = 0          # steps completed (barrier() calls)
         self.limit_ns = barrier_limit_ns
 
-    def barrier(self, stream=None):
-        """Stream-ordered: work after it on this rank's stream sees every rank's gather writes
-        issued before their barriers.  Every rank calls it once per step."""
+    @property
+    def step_buf(self) -> int:
+        """Index of the buffer the next step writes."""
+        return self.steps % 2
+
+    @property
+    def dst(self):
+        return self._dst[self.step_buf]
+
+    @property
+    def dst_c(self):
+        return self._dst_c[self.step_buf]
+
+    @property
+    def out(self):
+        """This rank's buffer holding the result of the last completed step."""
+        return self.bufs[(self.steps - 1) % 2] if self.steps > 0 else self.bufs[0]
+
+    def sync(self, stream=None):
+        """A flag barrier that does not end a step: every rank's work queued before it (on
+        the stream given) is complete before work after it runs on any rank.  Collective; e.g.
+        after each rank re-initialises the buffer the next step writes."""
         import blackhole_b200 as bh
 
         self.epoch += 1
         bh.peer_barrier(self.flags_c, self.world, self.rank, self.epoch, self.limit_ns,
                         stream=stream)
+
+    def barrier(self, stream=None):
+        """Ends a step (stream-ordered): work after it on this rank's stream sees every rank's
+        gather writes of this step.  Every rank calls it once per step, after the step's
+        gather call."""
+        self.sync(stream)
+        self.steps += 1
 
     def close(self):
         import blackhole_b200 as bh
@@ -139,14 +180,16 @@ class GatheredOutput:
         for p in self._mapped:
             bh.ipc_close(p)
         self._mapped = []
-        self.dst = [self.out]
-        self.dst_c = bh.pointer_array(self.dst)
+        self._dst = [[b] for b in self.bufs]
+        self._dst_c = [bh.pointer_array(d) for d in self._dst]
 
 
 def nsplit_gemm_gathered(M: int, N: int, K: int, A, SFA, B, SFB, alpha: float, rank: int,
                          world: int, out: GatheredOutput, stream=None):
-    """This rank's N-slice with the gather fused into the GEMM: afterwards (and after the
-    barrier it ends with) every rank's `out.out` holds the whole row-major M x N result."""
+    """One step of the N-split with the gather fused into the GEMM: this rank's N-slice goes
+    to the step's buffer on every rank, then the step's barrier.  Returns this rank's buffer,
+    which (for work after the call on `stream`) holds the whole row-major M x N result until
+    the step after next overwrites it (GatheredOutput)."""
     import blackhole_b200 as bh
 
     if out.M != M or out.N != N:

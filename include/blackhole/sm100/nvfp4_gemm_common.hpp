@@ -328,7 +328,8 @@ inline cudaError_t make_d_tmap(CUtensorMap* m, void* base, int64_t rows, int64_t
 }
 
 struct DeviceState {
-  std::once_flag once;
+  std::mutex mu;
+  bool ready = false;               // set once, under mu, after a successful set-up
   cudaError_t init_err = cudaSuccess;
   int num_sms = 0;
   uint32_t* status = nullptr;
@@ -339,20 +340,31 @@ inline DeviceState& device_state(int dev) {
   return states[dev & 63];
 }
 
-// Per-device one-time set-up (the reference keeps a process-wide static bool instead,
-// nvfp4_gemm.hpp:625-631, which misses every device after the first).
+// Per-device set-up (the reference keeps a process-wide static bool instead,
+// nvfp4_gemm.hpp:625-631, which misses every device after the first).  Only a successful
+// set-up is kept: after a failure (for instance a first call made while the stream is being
+// captured, where cudaGetSymbolAddress is not allowed) the returned state carries the error
+// and the next call tries again.
 inline DeviceState* prepare_device() {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
   DeviceState& st = device_state(dev);
-  std::call_once(st.once, [&]() {
-    st.init_err = cudaDeviceGetAttribute(&st.num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (st.init_err != cudaSuccess) return;
-    void* sym = nullptr;
-    st.init_err = cudaGetSymbolAddress(&sym, g_status);
-    st.status = static_cast<uint32_t*>(sym);
-  });
+  std::lock_guard<std::mutex> lock(st.mu);
+  if (st.ready) return &st;
+  int sms = 0;
+  void* sym = nullptr;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e == cudaSuccess) e = cudaGetSymbolAddress(&sym, g_status);
+  if (e != cudaSuccess) {
+    thread_local DeviceState failed;   // this call's error; the shared state stays unset
+    failed.init_err = e;
+    return &failed;
+  }
+  st.num_sms = sms;
+  st.status = static_cast<uint32_t*>(sym);
+  st.init_err = cudaSuccess;
+  st.ready = true;
   return &st;
 }
 

@@ -23,8 +23,11 @@
 //
 // Each CTA parks at most one partial, so the workspace is 8 flags per CTA plus
 // grid * MPAD * 128 * 4 bytes of partials (nvfp4_skinny_workspace_bytes).
-// Flags are raised to 1 by the producer of a partial and reset to 0 by its consumer, so a
-// workspace is reusable by later launches on the same stream (and by graph replays).
+// A flag is raised by the producer of a partial to its launch's tag and reset to 0 by its
+// consumer; the tag is odd and changes with every launch (a generation word next to the ticket
+// counter, advanced once per launch), so a flag that a launch left raised because it gave up on
+// a bounded wait never matches a later launch's tag: the workspace stays reusable by later
+// launches on the same stream (and by graph replays) after an aborted one too.
 // Because finishers wait only on lower-numbered CTAs, which were launched no later, the
 // dependency never points at a CTA that cannot be resident.
 // =====================================================================================
@@ -130,8 +133,10 @@ struct Nvfp4SkinnyParams {
   uint16_t* peer_d[kMaxGatherPeers];
   float* ws;            // [grid][MPAD][128] partials
   uint32_t* flags;      // [grid][8]: one per epilogue warp
-  uint32_t* ticket;     // entry counter: CTAs take ranges in the order they start
+  uint32_t* ticket;     // [0]: entry counter, CTAs take ranges in the order they start;
+                        // [1]: launch generation, advanced once per launch
   uint32_t* status;
+  uint64_t partial_wait_ns;   // bound of a finisher's wait for a partial (kWaitLimitNs)
   float alpha;
   int M, N, K;
   int kt_per_rb;        // units per 128-row block: ceil(K / UnitK)
@@ -236,6 +241,7 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
   volatile int* const abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   volatile uint32_t* const ticket_slot = reinterpret_cast<volatile uint32_t*>(tmem_slot + 2);
+  volatile uint32_t* const gen_slot = reinterpret_cast<volatile uint32_t*>(tmem_slot + 3);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -244,12 +250,20 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
     // Ranges go to CTAs in the order they start.  The taker of the last ticket resets the
     // counter for the next launch; that launch starts taking tickets only after every CTA of
     // this one has passed pdl_launch_dependents below, i.e. after the reset.
+    // The generation is read before the ticket is taken and advanced by the last taker after
+    // its reset, so every CTA of a launch reads the same value (the fences order the read, the
+    // ticket and the advance) and the next launch reads the advanced one.
+    const uint32_t gen = ld_acquire(p.ticket + 1);
+    __threadfence();
     const uint32_t t = atomicAdd(p.ticket, 1u);
     if (t == uint32_t(p.grid) - 1u) {
       atomicExch(p.ticket, 0u);
       __threadfence();
+      atomicExch(p.ticket + 1, gen + 1u);
+      __threadfence();
     }
     *ticket_slot = t;
+    *gen_slot = (gen << 1) | 1u;
     for (int s = 0; s < S; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
@@ -276,6 +290,7 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int c = static_cast<int>(*ticket_slot);
+  const uint32_t tag = *gen_slot;   // this launch's flag value (odd, never 0)
   pdl_launch_dependents();  // the next kernel may claim SMs as ours exit
   // The previous kernel in the stream must be complete before any operand or the workspace is
   // read or written; the producer first issues L2 prefetches of B / SFB.
@@ -455,9 +470,9 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
         int ready = 1;
         if (lane == 0) {
           const uint64_t t0 = globaltimer_ns();
-          while (ld_acquire(flag) == 0u) {
+          while (ld_acquire(flag) != tag) {
             if (*abort_flag) { ready = 0; break; }
-            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            if (globaltimer_ns() - t0 > p.partial_wait_ns) {
               *abort_flag = 1;
               if (p.status) atomicOr(p.status, kStatusEpilogueTimeout);
               ready = 0;
@@ -528,7 +543,7 @@ __global__ void __launch_bounds__(KT::NumThreads, 1)
           if (m0 + m < p.M) __stcg(dst + m * 128, v[m]);
         __threadfence();
         __syncwarp();
-        if (lane == 0) st_release(p.flags + kSkinnyFlagsPerCta * c + fi, 1u);
+        if (lane == 0) st_release(p.flags + kSkinnyFlagsPerCta * c + fi, tag);
         continue;
       }
       if constexpr (kEarlyPartials) {
@@ -570,7 +585,8 @@ inline cudaError_t launch_skinny(int M, int N, int K, const void* A, const void*
                                  const void* SFB, void* D, float alpha, void* ws, int64_t ws_bytes,
                                  int grid_cap, bool prefetch, DeviceState* st, cudaStream_t stream,
                                  int l2_prefetch_ktiles = KT::L2PrefetchKTiles,
-                                 int skew = KT::RangeSkew, const GatherSpec* g = nullptr) {
+                                 int skew = KT::RangeSkew, const GatherSpec* g = nullptr,
+                                 uint64_t partial_wait_ns = ptx::kWaitLimitNs) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -615,6 +631,7 @@ inline cudaError_t launch_skinny(int M, int N, int K, const void* A, const void*
   p.ticket = p.flags + kSkinnyFlagsPerCta * st->num_sms;
   p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + nvfp4_skinny_flag_bytes(st->num_sms));
   p.status = st->status;
+  p.partial_wait_ns = partial_wait_ns;
   p.alpha = alpha;
   p.M = M;
   p.N = N;
@@ -637,7 +654,8 @@ inline cudaError_t launch_skinny(int M, int N, int K, const void* A, const void*
 
 // Skinny-M GEMM with a caller-provided workspace of at least
 // nvfp4_skinny_workspace_bytes(num_SMs, nvfp4_skinny_mpad(M)) bytes, zero-filled before its
-// first use (the flag words must start at 0; every launch leaves them at 0).  M in [1, 128].
+// first use; every launch, one that gave up on a bounded wait included, leaves it usable by
+// the next launch on the stream.  M in [1, 128].
 //
 // With prefetch the kernel, launched as a programmatic dependent of the previous kernel in
 // the stream, issues L2 prefetches of the first B / SFB tiles of its range while that kernel
@@ -650,7 +668,8 @@ inline cudaError_t block_scaled_bf16_gemm_skinny(int M, int N, int K, void const
                                                  int64_t workspace_bytes,
                                                  cudaStream_t stream = nullptr,
                                                  int grid_cap = 1 << 30, bool prefetch = true,
-                                                 const detail::GatherSpec* g = nullptr) {
+                                                 const detail::GatherSpec* g = nullptr,
+                                                 uint64_t partial_wait_ns = ptx::kWaitLimitNs) {
   cudaError_t e = nvfp4_check_args(M, N, K, A, SFA, B, SFB, D);
   if (e != cudaSuccess) return e;
   e = detail::format_check_args<Fmt>(K, B);
@@ -664,19 +683,23 @@ inline cudaError_t block_scaled_bf16_gemm_skinny(int M, int N, int K, void const
     case 16:
       return detail::launch_skinny<Nvfp4SkinnyTraits<16, Fmt>>(
           M, N, K, A, SFA, B, SFB, D, alpha, workspace, workspace_bytes, grid_cap, prefetch, st, stream,
-          Nvfp4SkinnyTraits<16, Fmt>::L2PrefetchKTiles, Nvfp4SkinnyTraits<16, Fmt>::RangeSkew, g);
+          Nvfp4SkinnyTraits<16, Fmt>::L2PrefetchKTiles, Nvfp4SkinnyTraits<16, Fmt>::RangeSkew, g,
+          partial_wait_ns);
     case 32:
       return detail::launch_skinny<Nvfp4SkinnyTraits<32, Fmt>>(
           M, N, K, A, SFA, B, SFB, D, alpha, workspace, workspace_bytes, grid_cap, prefetch, st, stream,
-          Nvfp4SkinnyTraits<32, Fmt>::L2PrefetchKTiles, Nvfp4SkinnyTraits<32, Fmt>::RangeSkew, g);
+          Nvfp4SkinnyTraits<32, Fmt>::L2PrefetchKTiles, Nvfp4SkinnyTraits<32, Fmt>::RangeSkew, g,
+          partial_wait_ns);
     case 64:
       return detail::launch_skinny<Nvfp4SkinnyTraits<64, Fmt>>(
           M, N, K, A, SFA, B, SFB, D, alpha, workspace, workspace_bytes, grid_cap, prefetch, st, stream,
-          Nvfp4SkinnyTraits<64, Fmt>::L2PrefetchKTiles, Nvfp4SkinnyTraits<64, Fmt>::RangeSkew, g);
+          Nvfp4SkinnyTraits<64, Fmt>::L2PrefetchKTiles, Nvfp4SkinnyTraits<64, Fmt>::RangeSkew, g,
+          partial_wait_ns);
     default:
       return detail::launch_skinny<Nvfp4SkinnyTraits<128, Fmt>>(
           M, N, K, A, SFA, B, SFB, D, alpha, workspace, workspace_bytes, grid_cap, prefetch, st, stream,
-          Nvfp4SkinnyTraits<128, Fmt>::L2PrefetchKTiles, Nvfp4SkinnyTraits<128, Fmt>::RangeSkew, g);
+          Nvfp4SkinnyTraits<128, Fmt>::L2PrefetchKTiles, Nvfp4SkinnyTraits<128, Fmt>::RangeSkew, g,
+          partial_wait_ns);
   }
 }
 

@@ -15,7 +15,7 @@
 extern "C" {
 #endif
 
-#define BLACKHOLE_SM100_ABI_VERSION 5
+#define BLACKHOLE_SM100_ABI_VERSION 6
 
 #if defined(__GNUC__)
 #define BLACKHOLE_SM100_API __attribute__((visibility("default")))
@@ -53,9 +53,10 @@ BLACKHOLE_SM100_API int blackhole_sm100_nvfp4_bf16_gemm(int M, int N, int K, con
  * 2 = two-SM 256x256 tiles (cta_group::2), 3 = skinny-M stream-K (M <= 128),
  * 4 = skinny-M stream-K without the early L2 prefetch (same results).
  * workspace: device memory for the skinny schedule, at least
- * blackhole_sm100_workspace_bytes(M, N, K) bytes, zero-filled before its first use and left
- * zeroed by every call; NULL selects a library-owned buffer per (device, stream), allocated
- * on first use.  Calls that share one workspace must be ordered (same stream). */
+ * blackhole_sm100_workspace_bytes(M, N, K) bytes, zero-filled before its first use; every
+ * call leaves it ready for the next, a call that gave up on a bounded wait included; NULL
+ * selects a library-owned buffer per (device, stream), allocated on first use.  Calls that
+ * share one workspace must be ordered (same stream). */
 BLACKHOLE_SM100_API int blackhole_sm100_nvfp4_bf16_gemm_ex(int M, int N, int K, const void* A,
                                                            const void* SFA, const void* B,
                                                            const void* SFB, void* D, float alpha,
@@ -99,7 +100,8 @@ BLACKHOLE_SM100_API int blackhole_sm100_nvfp4_quantize(const void* X, int x_is_b
  * fixed 1,316,096-byte array inside this library, sized for M <= 16 on devices with at most
  * 160 SMs; larger M or more SMs return cudaErrorInvalidValue.  It calls no cudaMalloc or
  * cudaFree.  The first call on each device looks up the array's device address with
- * cudaGetSymbolAddress; make that first call before any stream capture.  Every call uses the
+ * cudaGetSymbolAddress; make that first call before any stream capture (a lookup that fails,
+ * inside a capture for instance, is not kept: the next call tries again).  Every call uses the
  * same array and clears its flag words first (cudaMemsetAsync on `stream`), so calls that
  * overlap on the GPU (different streams, or different host threads) race with each other. */
 BLACKHOLE_SM100_API int blackhole_sm100_nvfp4_bf16_gemm_noalloc(int M, int N, int K, const void* A,
@@ -154,6 +156,19 @@ BLACKHOLE_SM100_API int blackhole_sm100_peer_barrier(void* const* flags, int wor
  * Asynchronous on `stream`; read the status with blackhole_sm100_device_status. */
 BLACKHOLE_SM100_API int blackhole_sm100_selftest_bounded_wait(uint64_t limit_ns, uint64_t* result,
                                                               cudaStream_t stream);
+
+/* Self-test hook of the skinny schedule's recovery (no counterpart in the reference): the
+ * NVFP4 GEMM on the skinny schedule with a caller workspace, as blackhole_sm100_nvfp4_bf16_gemm_ex
+ * with schedule 3, except that a finishing CTA waits at most partial_wait_ns
+ * (0 < partial_wait_ns <= 4e9) for the partial sums of the CTAs sharing its row block.  With a
+ * bound far below a launch's duration the finishers give up: status bit 2 is set, their
+ * output rows are left unwritten and flags of the workspace stay raised.  The next launch on
+ * the same workspace must still compute the right result (the flags carry a per-launch tag):
+ * tests/test_bounded_wait_gpu.py checks that, without faulting anything. */
+BLACKHOLE_SM100_API int blackhole_sm100_selftest_skinny_partial_wait(
+    int M, int N, int K, const void* A, const void* SFA, const void* B, const void* SFB, void* D,
+    float alpha, void* workspace, int64_t workspace_bytes, uint64_t partial_wait_ns,
+    cudaStream_t stream);
 
 /* MXFP4 x MXFP4 -> BF16 (OCP Microscaling v1.0: E2M1 elements, one UE8M0 scale per 32
  * elements along K, in the same 128x4 blocked layout with 32-element groups).  No

@@ -433,11 +433,99 @@ void bho_gemm_ref_sampled(int64_t M, int64_t N, int64_t K, const uint8_t* A,
                            nthreads);
 }
 
-double bho_tolerance(float ref, float got, float alpha, int64_t K, double absdot) {
+static double bf16_ulp_of(float ref, float got) {
   float a = fabsf(ref) > fabsf(got) ? fabsf(ref) : fabsf(got);
   if (!(a >= 1.1754943508222875e-38f)) a = 1.1754943508222875e-38f;
   int e;
   frexp((double)a, &e);                  /* a in [2^(e-1), 2^e) */
-  double ulp = ldexp(1.0, (e - 1) - 7);  /* bf16 keeps 7 fraction bits */
-  return ulp + fabs((double)alpha) * (double)K * 0x1.0p-24 * absdot;
+  return ldexp(1.0, (e - 1) - 7);        /* bf16 keeps 7 fraction bits */
+}
+
+double bho_tolerance(float ref, float got, float alpha, int64_t K, double absdot) {
+  return bf16_ulp_of(ref, got) + fabs((double)alpha) * sqrt((double)K) * 0x1.0p-24 * absdot;
+}
+
+double bho_tolerance_worst(float ref, float got, float alpha, int64_t K, double absdot) {
+  return bf16_ulp_of(ref, got) + fabs((double)alpha) * (double)K * 0x1.0p-24 * absdot;
+}
+
+/* ------------------------------------------------------------------------------------ */
+/* The example's host loop in its own form (example/nvfp4_bf16_gemm.cu:159-168): element  */
+/* values and per-group scale values as float arrays built before the loop, and inside it */
+/* a = vA*sA, b = vB*sB, acc += a*b in k order.                                            */
+/* ------------------------------------------------------------------------------------ */
+void bho_decode_operand(int fmt_kind, const uint8_t* P, const uint8_t* SF, int64_t rows,
+                        int64_t K, float* vals, float* scales) {
+  const int vs = fmt_kind == 0 ? 16 : 32;
+  const int64_t kg = K / vs;
+  for (int64_t r = 0; r < rows; ++r) {
+    for (int64_t g = 0; g < kg; ++g)
+      scales[r * kg + g] = fmt_kind == 0 ? bho_ue4m3_to_float(SF[bho_sf_offset(r, g, K)])
+                                         : bho_ue8m0_to_float(SF[bho_sf_offset_vs(r, g, K, 32)]);
+    if (fmt_kind == 2) {
+      for (int64_t k = 0; k < K; ++k) vals[r * K + k] = bho_e4m3_to_float(P[r * K + k]);
+    } else {
+      const uint8_t* p = P + r * (K / 2);
+      for (int64_t k = 0; k < K; k += 2) {
+        vals[r * K + k] = bho_e2m1_to_float(p[k / 2] & 0xF);
+        vals[r * K + k + 1] = bho_e2m1_to_float(p[k / 2] >> 4);
+      }
+    }
+  }
+}
+
+typedef struct {
+  int64_t N, K, vs, m0, m1;
+  const float *vA, *sA, *vB, *sB;
+  float alpha;
+  uint16_t* D;
+} loop_job;
+
+/* One output row against every row of B; VS is a compile-time constant as in the example
+ * (k / KT::SFVecSize), so the group index is a shift, not a division. */
+#define BHO_LOOP_ROWS(VS)                                                         \
+  for (int64_t m = j->m0; m < j->m1; ++m) {                                       \
+    const float* va = j->vA + m * K;                                              \
+    const float* sa = j->sA + m * (K / (VS));                                     \
+    for (int64_t n = 0; n < j->N; ++n) {                                          \
+      const float* vb = j->vB + n * K;                                            \
+      const float* sb = j->sB + n * (K / (VS));                                   \
+      float acc = 0.f;                                                            \
+      for (int64_t k = 0; k < K; ++k) {                                           \
+        float a = va[k] * sa[k / (VS)];                                           \
+        float b = vb[k] * sb[k / (VS)];                                           \
+        acc += a * b;                                                             \
+      }                                                                           \
+      j->D[m * j->N + n] = bho_bf16_from_float(j->alpha * acc);                   \
+    }                                                                             \
+  }
+
+static void* loop_worker(void* arg) {
+  loop_job* j = (loop_job*)arg;
+  const int64_t K = j->K;
+  if (j->vs == 16) {
+    BHO_LOOP_ROWS(16)
+  } else {
+    BHO_LOOP_ROWS(32)
+  }
+  return NULL;
+}
+
+void bho_ref_loop(int64_t M, int64_t N, int64_t K, int vs, const float* vA, const float* sA,
+                  const float* vB, const float* sB, float alpha, uint16_t* D, int nthreads) {
+  if (nthreads < 1) nthreads = 1;
+  if (nthreads > 256) nthreads = 256;
+  if (nthreads > M) nthreads = (int)(M > 0 ? M : 1);
+  pthread_t tid[256];
+  loop_job jobs[256];
+  for (int t = 0; t < nthreads; ++t) {
+    loop_job j = {N, K, vs, M * t / nthreads, M * (t + 1) / nthreads, vA, sA, vB, sB, alpha, D};
+    jobs[t] = j;
+  }
+  if (nthreads == 1) {
+    loop_worker(&jobs[0]);
+    return;
+  }
+  for (int t = 0; t < nthreads; ++t) pthread_create(&tid[t], NULL, loop_worker, &jobs[t]);
+  for (int t = 0; t < nthreads; ++t) pthread_join(tid[t], NULL);
 }

@@ -103,11 +103,30 @@ void bho_gemm_ref_sampled_fmt(int fmt, int64_t M, int64_t N, int64_t K, const ui
                               float alpha, int64_t S, const int64_t* ms, const int64_t* ns,
                               uint16_t* D_out, double* absdot, int nthreads);
 
-/* Tolerance bound for one element:
- *   ulp_bf16(max(|ref|,|got|)) + |alpha| * K * 2^-24 * absdot
- * i.e. one BF16 ulp of the output plus the worst-case FP32 reassociation error of a
- * K-term sum (the products themselves are exact in FP32). */
+/* Tolerance for one element, the one every parity test asserts:
+ *   ulp_bf16(max(|ref|,|got|)) + |alpha| * sqrt(K) * 2^-24 * absdot
+ * One BF16 ulp of the output (two FP32 sums that differ in their last bits may round to
+ * neighbouring BF16 values) plus FP32 reassociation slack.  The products are exact in FP32,
+ * so the two sums differ only by rounding: at most K*2^-24*absdot in the worst case, and
+ * about sqrt(K)*2^-24 times the size of the partial sums when the rounding errors have
+ * random signs, which is what the slack allows (the worst-case form is 169x looser at
+ * K = 28672 and lets most elements of a result with a 256-deep k-tile missing through). */
 double bho_tolerance(float ref, float got, float alpha, int64_t K, double absdot);
+/* The worst-case bound, ulp_bf16 + |alpha| * K * 2^-24 * absdot: the outer limit, reported. */
+double bho_tolerance_worst(float ref, float got, float alpha, int64_t K, double absdot);
+
+/* ---- the example's host loop in its own form (example/nvfp4_bf16_gemm.cu:159-168) ---- */
+/* Decodes an operand into element values vals[rows*K] and scale values
+ * scales[rows*(K/vs)] (fmt_kind 0 NVFP4 vs = 16, 1 MXFP4 vs = 32, 2 MXFP8 vs = 32): the float
+ * arrays the example builds before its loop (refA / sfaVal). */
+void bho_decode_operand(int fmt_kind, const uint8_t* P, const uint8_t* SF, int64_t rows,
+                        int64_t K, float* vals, float* scales);
+/* D[m,n] = bf16(alpha * acc), acc += (vA*sA)*(vB*sB) over k in order, every row m of A
+ * against every row n of B, rows split over nthreads threads.  Same bits as
+ * bho_gemm_ref_full (each product is exact in FP32); this is the loop the CPU baselines time,
+ * with the decoding done before it as in the example. */
+void bho_ref_loop(int64_t M, int64_t N, int64_t K, int vs, const float* vA, const float* sA,
+                  const float* vB, const float* sB, float alpha, uint16_t* D, int nthreads);
 
 #ifdef __cplusplus
 }

@@ -48,7 +48,7 @@ def check_full(M, N, K, A, SFA, B, SFB, alpha, got):
     return O.check(ref, got, alpha, K, ad), ref
 
 
-def check_sampled(M, N, K, A, SFA, B, SFB, alpha, got, S=4096, seed=7):
+def check_sampled(M, N, K, A, SFA, B, SFB, alpha, got, S=4096, seed=7, record=True):
     rng = np.random.default_rng(seed)
     ms = rng.integers(0, M, S)
     ns = rng.integers(0, N, S)
@@ -56,4 +56,4 @@ def check_sampled(M, N, K, A, SFA, B, SFB, alpha, got, S=4096, seed=7):
     ms[:4] = [0, 0, M - 1, M - 1]
     ns[:4] = [0, N - 1, 0, N - 1]
     ref, ad = O.gemm_sampled(M, N, K, A, SFA, B, SFB, ms, ns, alpha)
-    return O.check(ref, got[ms, ns], alpha, K, ad)
+    return O.check(ref, got[ms, ns], alpha, K, ad, record=record)

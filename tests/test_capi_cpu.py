@@ -34,7 +34,7 @@ def test_library_exports_every_declared_symbol():
     L = bh.load()
     for s in syms:
         assert hasattr(L, s)
-    assert L.blackhole_sm100_abi_version() == 5
+    assert L.blackhole_sm100_abi_version() == 6
     assert "blackhole_sm100_mxfp4_bf16_gemm_ex" in syms and "blackhole_sm100_mxfp4_quantize" in syms
 
 
