@@ -58,9 +58,10 @@ def parse():
     ap.add_argument("--n", type=int, default=8192, help="columns per GPU")
     ap.add_argument("--k", type=int, default=8192)
     ap.add_argument("--no-decode", action="store_true")
-    ap.add_argument("--case", default="all", choices=["all", "main", "decode"],
-                    help="main: only the 8192^3-class GEMM; decode: only the M=16 GEMM "
-                         "(small runs for profiler captures; the JSON line then lacks the other)")
+    ap.add_argument("--case", default="all", choices=["all", "main", "decode", "quantize"],
+                    help="main: only the 8192^3-class GEMM; decode: only the M=16 GEMM; "
+                         "quantize: only the quantiser leg (small runs for profiler captures; "
+                         "the JSON line then lacks the others)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--decode-warmup", type=int, default=4000,
                     help="decode warm-up launches (~0.1 s at 4000; fewer for profiler captures)")
@@ -572,6 +573,43 @@ def run_mx(args, dev, rank, world, fp4_peak, hbm_peak, fmt="mxfp4"):
     return out
 
 
+def run_quantize(args, dev, world, hbm_peak, rows=28672, K=8192):
+    """The NVFP4 quantiser (the step before the GEMM) on configs[2]'s weight shape, FP32 input
+    (940 MB > L2), calls back to back.  One call is two HBM passes over X -- the tensor amax,
+    then the quantiser proper -- so its minimal traffic is 2 reads of X plus the codes and
+    scale factors written; `frac` is that traffic's rate over the measured HBM peak."""
+    import torch
+    import blackhole_b200 as bh
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(99)
+    x = torch.randn((rows, K), generator=g, device=dev, dtype=torch.float32)
+    packed = torch.empty((rows, K // 2), dtype=torch.uint8, device=dev)
+    sf = torch.empty(bh.sf_storage_bytes(rows, K), dtype=torch.uint8, device=dev)
+    scales = torch.empty(2, dtype=torch.float32, device=dev)
+    steps = max(5, min(args.steps, 50))
+    for _ in range(3):
+        bh.nvfp4_quantize(x, rows, K, packed, sf, scales)
+    barrier(world)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        bh.nvfp4_quantize(x, rows, K, packed, sf, scales)
+    e.record()
+    barrier(world)
+    ms = max_over_ranks(s.elapsed_time(e) / steps, world)
+    read = rows * K * 4
+    written = rows * K // 2 + sf_bytes(rows, K)
+    traffic = 2 * read + written
+    del x, packed, sf, scales
+    return {"workload": f"{rows} x {K} FP32 -> NVFP4 (packed E2M1 + UE4M3 128x4 scale factors)",
+            "ms_per_call": ms, "steps": steps,
+            "gbs_two_pass": traffic / (ms * 1e-3) / 1e9, "frac": traffic / (ms * 1e-3) / 1e9 / hbm_peak,
+            "bytes_per_call": {"read_x_twice": 2 * read, "written": written},
+            "gbs_one_read": (read + written) / (ms * 1e-3) / 1e9,
+            "launches_per_call": 2, "peak": hbm_peak}
+
+
 def run_prefill(args, dev, rank, world, fp4_peak):
     """M=16384 N=8192 K=28672, A from N(0,1) with 1% of entries x20, B from
     N(0, 0.02^2); 2 rotating input sets (~800 MB), back to back."""
@@ -840,6 +878,16 @@ def main():
             dist.barrier()
             dist.destroy_process_group()
         return
+    if args.case == "quantize":
+        q = run_quantize(args, dev, world, hbm_peak)
+        if rank == 0:
+            print(json.dumps({"case": "quantize", "quantize": q,
+                              "gpu_launches": 2 * (q["steps"] + 3)}), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if args.case == "main":
         args.no_decode = True
         args.no_configs = True
@@ -897,6 +945,8 @@ def main():
         result["gpu_launches"] += result["decode"]["steps"] * len(result["decode"]["sweep_by_M"])
 
     if not args.no_configs:
+        result["quantize"] = run_quantize(args, dev, world, hbm_peak)
+        result["gpu_launches"] += 2 * result["quantize"]["steps"]
         result["prefill"] = run_prefill(args, dev, rank, world, fp4_peak)
         result["nsplit"] = run_nsplit(args, dev, rank, world, fp4_peak)
         result["gpu_launches"] += result["prefill"]["steps"] + result["nsplit"]["steps"]

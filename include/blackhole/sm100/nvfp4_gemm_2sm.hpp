@@ -33,7 +33,7 @@
 
 namespace blackhole::sm100 {
 
-template <int Stages_ = 5, class Fmt_ = Nvfp4Format>
+template <int Stages_ = 5, class Fmt_ = Nvfp4Format, bool OverlapAcc_ = false>
 struct Nvfp4Gemm2SmTraitsT {
   using Fmt = Fmt_;
   using Geo = BlockScaleGeometry<Fmt>;
@@ -64,7 +64,16 @@ struct Nvfp4Gemm2SmTraitsT {
   // are then copied by a warp of their own into SfBufs TMEM buffers, up to SfBufs k-tiles
   // ahead of the MMAs (measured on B200 at 8192^3: 5% fewer cycles, 2.5% less time at the
   // power cap; for MXFP4 the handoff costs more than it saves, so its MMA warp copies).
-  static constexpr bool SfCopyWarp = Fmt::SfVec == 16;
+  //
+  // OverlapAcc: two accumulator stages that share AccOverlap columns of TMEM (stage s at
+  // column s * AccStageStride), one tile per stage in turn, and one scale-factor buffer after
+  // them, copied by the MMA warp right before each k-tile's MMAs.  The epilogue reads the
+  // shared columns first and releases the accumulator as soon as they are in registers, so the
+  // next tile's MMAs start while the epilogue still drains the rest of the previous one.
+  static constexpr bool OverlapAcc = OverlapAcc_;
+  static constexpr uint32_t AccOverlap = 64;
+  static constexpr uint32_t AccStageStride = 256 - AccOverlap;
+  static constexpr bool SfCopyWarp = Fmt::SfVec == 16 && !OverlapAcc;
   static constexpr int SfBufs = SfCopyWarp ? 4 : 1;
   static constexpr int NumWarps = SfCopyWarp ? 11 : 10;
   static constexpr int NumThreads = NumWarps * 32;
@@ -78,7 +87,7 @@ struct Nvfp4Gemm2SmTraitsT {
   // then SFB (8 per k-step).
   static constexpr uint32_t TmemCols = 512;
   static constexpr uint32_t AccCol = 0;
-  static constexpr uint32_t SfCol = 256;
+  static constexpr uint32_t SfCol = OverlapAcc ? AccStageStride + 256 : 256;
   static constexpr uint32_t SfStride = 12 * SfAtoms;
 
   // epilogue staging: one 32-row x 64-column BF16 box (4 KB, 128B-swizzled) per epilogue warp
@@ -301,17 +310,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
         }
       };
       for (int tile = cluster; ok && tile < p.num_tiles; tile += num_clusters) {
-        if (!wait_bounded_warp(acc_empty, acc_phase ^ 1u, abort_flag, p.status, kStatusMmaTimeout)) {
-          ok = false;
-          break;
+        // the tile's accumulator: one of the two overlapping stages in turn (OverlapAcc)
+        const uint32_t acc_col = KT::OverlapAcc ? (acc_phase ? KT::AccStageStride : 0u) : KT::AccCol;
+        if constexpr (KT::OverlapAcc) {
+          // first stage, then its scale factors, then the accumulator: the copies run while
+          // the epilogue is still releasing the previous tile's shared columns
+          if (!wait_bounded_warp(full_bar(stage), phase, abort_flag, p.status, kStatusMmaTimeout)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          copy_sf(stage, 0u);
+          issued_any = true;
+          if (!wait_bounded_warp(acc_empty, acc_phase ^ 1u, abort_flag, p.status, kStatusMmaTimeout)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        } else {
+          if (!wait_bounded_warp(acc_empty, acc_phase ^ 1u, abort_flag, p.status, kStatusMmaTimeout)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // the first stage of a tile is waited for; each later one is probed one k-tile ahead
+          if (!wait_bounded_warp(full_bar(stage), phase, abort_flag, p.status, kStatusMmaTimeout)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
         }
-        tc_fence_after();
-        // the first stage of a tile is waited for; each later one is probed one k-tile ahead
-        if (!wait_bounded_warp(full_bar(stage), phase, abort_flag, p.status, kStatusMmaTimeout)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
         for (int kt = 0; kt < p.k_tiles; ++kt) {
           const int nstage = stage + 1 == S ? 0 : stage + 1;
           const uint32_t nphase = stage + 1 == S ? (phase ^ 1u) : phase;
@@ -325,7 +353,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
               break;
             }
             tc_fence_after();
-          } else {
+          } else if (!KT::OverlapAcc || kt > 0) {
             copy_sf(stage, sfbuf);
           }
           const uint64_t adesc = desc_kmajor<KT::RowBytes>(sA + stage * KT::ABytes);
@@ -336,7 +364,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
             const int at = j / KT::StepsPerAtom;
             const uint32_t sid = KT::Geo::sf_id(j);   // byte in the entry
             tc_mma_bs_pair_w<typename KT::Fmt>(
-                tmem + KT::AccCol, adesc + 2 * j, bdesc + 2 * j, idesc_with_sf_id(idesc, sid),
+                tmem + acc_col, adesc + 2 * j, bdesc + 2 * j, idesc_with_sf_id(idesc, sid),
                 sf_tmem_addr(ta + 4 * at, sid), sf_tmem_addr(ta + 4 * KT::SfAtoms + 8 * at, sid),
                 (kt | j) != 0 ? 1u : 0u);
           }
@@ -414,7 +442,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
     // ------------------------------ epilogue (both CTAs) ----------------------------
     const int q = warp & 3;
     const int half = (warp - KT::FirstEpiWarp) >> 2;
-    const uint32_t t_row = tmem + (static_cast<uint32_t>(32 * q) << 16) + KT::AccCol + 128 * half;
     const uint32_t leader_acc_empty = mapa_shared(acc_empty, 0);
     uint32_t acc_phase = 0;
     for (int tile = cluster; tile < p.num_tiles; tile += num_clusters) {
@@ -427,18 +454,59 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
       // accumulator column n XOR 32 (32-column groups swapped pairwise inside each half; lanes
       // and halves as for kind::mxf4nvf4), so that kind reads the groups crosswise.
       constexpr uint32_t x = KT::Fmt::Kind == MmaKind::kMxf8f6f4 ? 32u : 0u;
-      tmem_ld_32x32b_x32(t_row + (0 ^ x), v0);
-      tmem_ld_32x32b_x32(t_row + (32 ^ x), v1);
-      tmem_ld_32x32b_x32(t_row + (64 ^ x), v2);
-      tmem_ld_32x32b_x32(t_row + (96 ^ x), v3);
-      tmem_ld_wait();
-      reg_fence(v0);
-      reg_fence(v1);
-      reg_fence(v2);
-      reg_fence(v3);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(leader_acc_empty);
+      const uint32_t acc_col = KT::OverlapAcc ? (acc_phase ? KT::AccStageStride : 0u) : KT::AccCol;
+      const uint32_t t_row = tmem + (static_cast<uint32_t>(32 * q) << 16) + acc_col + 128 * half;
+      if constexpr (KT::OverlapAcc) {
+        // Stage 0 shares its last 64 columns with stage 1, stage 1 its first 64 with stage 0.
+        // The warps of the half that holds them read those first and release the accumulator;
+        // the other half's warps release it at once (the next tile's MMAs never touch their
+        // columns, and the tile after that waits for their release of the next tile).
+        const bool shared_hi = acc_phase == 0u;
+        const bool holds = (half == 1) == shared_hi;
+        if (!holds) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(leader_acc_empty);
+        }
+        if (shared_hi) {
+          tmem_ld_32x32b_x32(t_row + (64 ^ x), v2);
+          tmem_ld_32x32b_x32(t_row + (96 ^ x), v3);
+        } else {
+          tmem_ld_32x32b_x32(t_row + (0 ^ x), v0);
+          tmem_ld_32x32b_x32(t_row + (32 ^ x), v1);
+        }
+        tmem_ld_wait();
+        if (holds) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(leader_acc_empty);
+        }
+        if (shared_hi) {
+          tmem_ld_32x32b_x32(t_row + (0 ^ x), v0);
+          tmem_ld_32x32b_x32(t_row + (32 ^ x), v1);
+        } else {
+          tmem_ld_32x32b_x32(t_row + (64 ^ x), v2);
+          tmem_ld_32x32b_x32(t_row + (96 ^ x), v3);
+        }
+        tmem_ld_wait();
+        reg_fence(v0);
+        reg_fence(v1);
+        reg_fence(v2);
+        reg_fence(v3);
+      } else {
+        tmem_ld_32x32b_x32(t_row + (0 ^ x), v0);
+        tmem_ld_32x32b_x32(t_row + (32 ^ x), v1);
+        tmem_ld_32x32b_x32(t_row + (64 ^ x), v2);
+        tmem_ld_32x32b_x32(t_row + (96 ^ x), v3);
+        tmem_ld_wait();
+        reg_fence(v0);
+        reg_fence(v1);
+        reg_fence(v2);
+        reg_fence(v3);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(leader_acc_empty);
+      }
       acc_phase ^= 1u;
 
       // alpha * acc -> BF16 -> this warp's swizzled staging box -> TMA store, 64 columns at

@@ -39,7 +39,7 @@
 
 namespace blackhole::sm100 {
 
-template <int MPAD_, class Fmt_ = Nvfp4Format>
+template <int MPAD_, class Fmt_ = Nvfp4Format, int KpsOverride_ = 0>
 struct Nvfp4SkinnyTraits {
   using Fmt = Fmt_;
   using Geo = BlockScaleGeometry<Fmt>;
@@ -55,7 +55,7 @@ struct Nvfp4SkinnyTraits {
   // (4-bit) or 16 KB (expanded) of weights; measured on B200 at N = 28672, K = 8192: M = 16
   // NVFP4 25.5 -> 23.7 us, MXFP4 24.1 -> 21.9 us, MXFP8 x MXFP4 39.0 -> 27.3 us.  Wider
   // activation tiles (MPAD >= 32) keep one k-tile per stage, where the ring depth matters more.
-  static constexpr int KPS = (Fmt::BExpand || MPAD <= 16) ? 2 : 1;
+  static constexpr int KPS = KpsOverride_ > 0 ? KpsOverride_ : ((Fmt::BExpand || MPAD <= 16) ? 2 : 1);
   static constexpr int UnitK = KPS * TileK;                 // K-elements per unit
   static constexpr int UnitSteps = KPS * KSteps;            // MMAs per unit
   static constexpr int TileWBytes = TileW * RowBytes;       // one k-tile of B: 16 KB

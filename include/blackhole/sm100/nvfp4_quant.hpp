@@ -13,7 +13,8 @@
 //
 // This is the step before the GEMM that the reference performs on the host with CUTLASS
 // converters (example/nvfp4_bf16_gemm.cu:60-71, :104-133).  Two HBM-bound kernels:
-// a grid-stride amax reduction, then one thread per 16-element block.
+// a grid-stride amax reduction, then the quantiser proper with four lanes per 16-element
+// block (coalesced 512-byte warp loads, 64-byte warp stores of codes).
 // =====================================================================================
 
 #include <algorithm>
@@ -123,46 +124,135 @@ __global__ void __launch_bounds__(256) amax_kernel(const T* __restrict__ x, int6
   }
 }
 
-// One thread per (row, 16-element group) over the layout's padded extent: rows padded to
-// 128 and groups to a multiple of 4; padding entries get s = 0.
-template <class T>
+// Four E2M1 codes of q[0..3] (round to nearest even, finite values past 6 saturate), q[0] in
+// the lowest nibble.  cvt...e2m1x2 puts its first source in the upper nibble.
+__device__ __forceinline__ uint32_t e2m1x4_cvt(float q0, float q1, float q2, float q3) {
+  uint32_t out;
+  asm("{\n\t.reg .b8 b0, b1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+      "mov.b32 %0, {b0, b1, b0, b1};\n\t}"
+      : "=r"(out)
+      : "f"(q0), "f"(q1), "f"(q2), "f"(q3));
+  return out & 0xFFFFu;
+}
+// UE4M3 code of v >= 0 (round to nearest even, saturating at 448): the E4M3 conversion of a
+// non-negative value, whose sign bit is then 0.
+__device__ __forceinline__ uint32_t ue4m3_cvt(float v) {
+  uint16_t d;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(d) : "f"(0.0f), "f"(v));
+  return d & 0xFFu;
+}
+
+// The recipe's roundings are of exact IEEE quotients: s = UE4M3(fl(fl(amax_b / 6) / g)) and
+// q = E2M1(fl(x / fl(s * g))).  Both conversions are monotone with rounding thresholds of few
+// significant bits (E2M1: the midpoints 0.25, 0.75, ..., 5, three bits; UE4M3: midpoints of
+// values with four, five bits), so they are computed from a cheap estimate y of the quotient
+// (products with reciprocals; within 6 units in the last place of the quotient) unless y lies
+// within 16 (E2M1) or 32 (UE4M3) representable floats of a value with that few significant
+// bits -- its low 21 (19) fraction bits, offset by the window, wrap into the window.  Then the
+// exact division is made.  A quotient that far from every threshold rounds like its estimate,
+// so the results are bit-identical to the plain recipe; the exact path runs for a few
+// elements in a million.
+__device__ __forceinline__ bool near_e2m1_threshold(float y) {
+  return ((__float_as_uint(y) + 16u) & 0x1FFFFFu) < 33u;
+}
+__device__ __forceinline__ bool near_ue4m3_threshold(float y) {
+  return ((__float_as_uint(y) + 32u) & 0x7FFFFu) < 65u;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+template <class T> struct Vec4In;
+template <> struct Vec4In<float> {
+  static __device__ __forceinline__ float4 load(const float* p) {
+    return __ldcs(reinterpret_cast<const float4*>(p));
+  }
+};
+template <> struct Vec4In<__nv_bfloat16> {
+  static __device__ __forceinline__ float4 load(const __nv_bfloat16* p) {
+    const uint2 v = __ldcs(reinterpret_cast<const uint2*>(p));
+    return make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xFFFF0000u),
+                       __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xFFFF0000u));
+  }
+};
+
+// Work item: 128 consecutive elements of one row (a segment), one warp, 4 elements per lane,
+// so one 16-element block is 4 neighbouring lanes.  Items run over the layout's padded rows
+// (a multiple of 128); items of padding rows and the groups past K of a row's last segment
+// write zero scale factors.  Every scale-factor write is one 4-byte word (4 groups of one row,
+// kg % 4 == 0 .. 3) by lane 0 or 16; codes are 16-bit stores, 64 contiguous bytes per warp.
+template <class T, int kUnroll>
 __global__ void __launch_bounds__(256) quantize_kernel(const T* __restrict__ x, int rows, int K,
                                                        uint8_t* __restrict__ packed,
                                                        uint8_t* __restrict__ sf,
                                                        float* __restrict__ scales) {
-  const int groups = K / 16;
-  const int groups_pad = (groups + 3) / 4 * 4;
-  const int64_t rows_pad = (int64_t(rows) + 127) / 128 * 128;
-  const int64_t idx = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;
-  if (idx >= rows_pad * groups_pad) return;
-  const int64_t r = idx / groups_pad;
-  const int64_t kg = idx - r * groups_pad;
+  const int lane = threadIdx.x & 31;
+  const int segs = (K + 127) / 128;
+  const int rows_pad = (rows + 127) / 128 * 128;
+  const int words_per_row = (K / 16 + 3) / 4;          // 4-group words (the padded groups)
+  const int items = rows_pad * segs;                   // < 2^31: checked by the launcher
+  const int warp0 = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int nwarps = static_cast<int>((gridDim.x * blockDim.x) >> 5);
   const float amax = scales[0];
-  const float g = amax / 2688.0f;
-  if (idx == 0) scales[1] = g;
-  uint32_t s_code = 0;
-  if (r < rows && kg < groups) {
-    float v[16];
-    load16(x + r * K + kg * 16, v);
-    float amax_b = 0.0f;
+  const float g = amax / 2688.0f;                       // amax / (448 * 6)
+  if (blockIdx.x == 0 && threadIdx.x == 0) scales[1] = g;
+  // (amax_b / 6) / g ~ amax_b * c: fl(1/6), fl(1/g) and their product, three roundings
+  const float c = __frcp_rn(6.0f) * __frcp_rn(g);
+
+  for (int base = warp0 * kUnroll; base < items; base += nwarps * kUnroll) {
+    float4 v[kUnroll];
+    int row[kUnroll], k0[kUnroll];
+    bool live[kUnroll];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) amax_b = fmaxf(amax_b, fabsf(v[i]));
-    float s_val = 0.0f;
-    if (g > 0.0f) {
-      s_code = ue4m3_rne((amax_b / 6.0f) / g);
-      s_val = ue4m3_value(s_code);
+    for (int u = 0; u < kUnroll; ++u) {          // every load of the unrolled items first
+      const int it = base + u;
+      const int r = it / segs;                    // warp-uniform
+      const int seg = it - r * segs;
+      row[u] = r;
+      k0[u] = seg * 128 + lane * 4;
+      live[u] = it < items && r < rows && k0[u] < K;
+      v[u] = live[u] ? Vec4In<T>::load(x + int64_t(r) * K + k0[u]) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    const float scale = s_val * g;
-    uint32_t lo = 0, hi = 0;
-    if (s_val != 0.0f) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) lo |= e2m1_rne(v[i] / scale) << (4 * i);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) hi |= e2m1_rne(v[8 + i] / scale) << (4 * i);
+    for (int u = 0; u < kUnroll; ++u) {
+      if (base + u >= items) break;               // warp-uniform
+      float m = fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)), fmaxf(fabsf(v[u].z), fabsf(v[u].w)));
+      m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
+      m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 2));   // the block's amax on its 4 lanes
+      uint32_t s_code = 0, codes = 0;
+      if (live[u] && g > 0.0f && m > 0.0f) {
+        const float ys = m * c;
+        s_code = near_ue4m3_threshold(ys) ? ue4m3_cvt((m / 6.0f) / g) : ue4m3_cvt(ys);
+        const float s_val = ue4m3_value(s_code);
+        if (s_val != 0.0f) {
+          const float scale = s_val * g;
+          const float rs = rcp_approx(scale);       // subnormal scale: inf, every y "near"
+          const float y0 = v[u].x * rs, y1 = v[u].y * rs, y2 = v[u].z * rs, y3 = v[u].w * rs;
+          if (near_e2m1_threshold(y0) || near_e2m1_threshold(y1) || near_e2m1_threshold(y2) ||
+              near_e2m1_threshold(y3))
+            codes = e2m1x4_cvt(v[u].x / scale, v[u].y / scale, v[u].z / scale, v[u].w / scale);
+          else
+            codes = e2m1x4_cvt(y0, y1, y2, y3);
+        }
+      }
+      if (live[u])
+        *reinterpret_cast<uint16_t*>(packed + (int64_t(row[u]) * K + k0[u]) / 2) =
+            static_cast<uint16_t>(codes);
+      // the 8 groups of the segment as two words: lanes 0, 4, 8, 12 and 16, 20, 24, 28
+      const int src = (lane & 16) + 4 * (lane & 3);
+      const uint32_t c = __shfl_sync(0xFFFFFFFFu, s_code, src) << (8 * (lane & 3));
+      uint32_t word = c;
+      word |= __shfl_xor_sync(0xFFFFFFFFu, word, 1);
+      word |= __shfl_xor_sync(0xFFFFFFFFu, word, 2);
+      const int w = (k0[u] - lane * 4) / 64 + (lane >> 4);   // this lane's word of the row
+      if ((lane & 15) == 0 && w < words_per_row)
+        *reinterpret_cast<uint32_t*>(sf + blackhole::sf_offset(row[u], 4 * w, K)) = word;
     }
-    *reinterpret_cast<uint2*>(packed + (r * K + kg * 16) / 2) = make_uint2(lo, hi);
   }
-  sf[blackhole::sf_offset(r, kg, K)] = static_cast<uint8_t>(s_code);
 }
 
 // MXFP4 (OCP MX v1.0): one thread per (row, 32-element group) over the padded extent.
@@ -282,18 +372,23 @@ inline cudaError_t nvfp4_quantize(const void* X, int x_is_bf16, int rows, int K,
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t n16 = int64_t(rows) * K / 16;
   const int amax_grid = static_cast<int>(std::min<int64_t>((n16 + 255) / 256, int64_t(sms) * 8));
-  const int64_t work = (int64_t(rows) + 127) / 128 * 128 * ((K / 16 + 3) / 4 * 4);
-  const int64_t qgrid = (work + 255) / 256;
-  if (qgrid > 0x7FFFFFFF) return cudaErrorInvalidValue;
+  // quantiser: 8 warps per CTA, 4 items (segments of 128 elements) per warp and pass,
+  // at most 8 CTAs per SM, striding over the items
+  constexpr int kUnroll = 4;
+  const int64_t items = (int64_t(rows) + 127) / 128 * 128 * ((K + 127) / 128);
+  if (items >= (int64_t(1) << 31) - (int64_t(1) << 20)) return cudaErrorInvalidValue;
+  const int qgrid = static_cast<int>(
+      std::max<int64_t>(1, std::min<int64_t>((items + 8 * kUnroll - 1) / (8 * kUnroll),
+                                             int64_t(sms) * 8)));
   if (x_is_bf16) {
     auto xp = static_cast<const __nv_bfloat16*>(X);
     quant_detail::amax_kernel<<<amax_grid, 256, 0, stream>>>(xp, n16, scales);
-    quant_detail::quantize_kernel<<<static_cast<int>(qgrid), 256, 0, stream>>>(
+    quant_detail::quantize_kernel<__nv_bfloat16, kUnroll><<<qgrid, 256, 0, stream>>>(
         xp, rows, K, static_cast<uint8_t*>(packed), static_cast<uint8_t*>(sf), scales);
   } else {
     auto xp = static_cast<const float*>(X);
     quant_detail::amax_kernel<<<amax_grid, 256, 0, stream>>>(xp, n16, scales);
-    quant_detail::quantize_kernel<<<static_cast<int>(qgrid), 256, 0, stream>>>(
+    quant_detail::quantize_kernel<float, kUnroll><<<qgrid, 256, 0, stream>>>(
         xp, rows, K, static_cast<uint8_t*>(packed), static_cast<uint8_t*>(sf), scales);
   }
   return cudaGetLastError();

@@ -55,3 +55,41 @@ def test_quantizer_all_zero_tensor():
     p, sf, sc = _run(x)
     assert sc[0] == 0 and sc[1] == 0
     assert not p.any() and not sf.any()
+
+
+def _tie_matrix():
+    """Blocks whose quotients sit exactly on rounding thresholds.  amax = 5.25 makes the global
+    scale g = 5.25 / 2688 = 2^-9 exact; a block with amax 25.5 * 2^-9 has (amax/6)/g = 4.25, a
+    UE4M3 midpoint (rounds to 4), so its scale is 4 * 2^-9 = 2^-7 and its elements t * 2^-7
+    divide to exactly t, every E2M1 midpoint and its negative; other blocks do the same at the
+    saturated scale 448 (scale 0.875) and put tiny values (codes 0 and negative 0) next to them."""
+    mids = [0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0]
+    rows, K = 4, 64
+    x = np.zeros((rows, K), np.float32)
+    s7 = 2.0 ** -7
+    x[0, :16] = [6.375 * s7] + [t * s7 for t in mids] + [-t * s7 for t in mids] + [0.0]
+    x[1, :16] = [5.25] + [t * 0.875 for t in mids] + [-t * 0.875 for t in mids] + [-1e-6]
+    x[2, 16:32] = [25.5 * 2.0 ** -9] + [-0.01 * s7, 0.01 * s7, -0.0] + [(i - 6) * 0.3 * s7 for i in range(12)]
+    x[3, :] = O.gen_normal(5, K, 0.0, 0.5)
+    return x
+
+
+def test_quantizer_ties_and_signed_zeros_bit_exact():
+    x = _tie_matrix()
+    p_ref, sf_ref, g_ref = O.quantize(x)
+    assert g_ref == 2.0 ** -9
+    p, sf, sc = _run(x)
+    assert sc[1] == np.float32(g_ref)
+    assert np.array_equal(sf, sf_ref)
+    assert np.array_equal(p, p_ref), np.nonzero(p != p_ref)
+
+
+def test_quantizer_large_ragged_bit_exact():
+    """Many rows (several passes of the persistent grid), K not a multiple of 128 (partial
+    last segments) and a row count that is not a multiple of 128 (padding rows)."""
+    rows, K = 1500, 2000 - 2000 % 16 + 16
+    x = O.gen_normal(123, rows * K, 0.0, 2.0).reshape(rows, K)
+    p_ref, sf_ref, g_ref = O.quantize(x)
+    p, sf, sc = _run(x)
+    assert sc[1] == np.float32(g_ref)
+    assert np.array_equal(sf, sf_ref) and np.array_equal(p, p_ref)
