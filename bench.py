@@ -58,10 +58,11 @@ def parse():
     ap.add_argument("--n", type=int, default=8192, help="columns per GPU")
     ap.add_argument("--k", type=int, default=8192)
     ap.add_argument("--no-decode", action="store_true")
-    ap.add_argument("--case", default="all", choices=["all", "main", "decode", "quantize"],
+    ap.add_argument("--case", default="all", choices=["all", "main", "decode", "quantize", "compare"],
                     help="main: only the 8192^3-class GEMM; decode: only the M=16 GEMM; "
-                         "quantize: only the quantiser leg (small runs for profiler captures; "
-                         "the JSON line then lacks the others)")
+                         "quantize: only the quantiser leg; compare: this library's and cuBLASLt's "
+                         "NVFP4 GEMM alternating on the same operands (small runs for profiler "
+                         "captures; the JSON line then lacks the others)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--decode-warmup", type=int, default=4000,
                     help="decode warm-up launches (~0.1 s at 4000; fewer for profiler captures)")
@@ -472,6 +473,41 @@ def library_baseline(M, N, K, sets, steps, warmup, world):
     return {"impl": "cuBLASLt NVFP4 block-scaled GEMM via torch._scaled_mm (comparison only)",
             "tflops": 2.0 * M * N * K * world / (ms * 1e-3) / 1e12, "ms_per_step": ms,
             "steps": steps, "clocks": clk.summary()}
+
+
+def run_compare(args, dev, M, N, K):
+    """--case compare: this library's GEMM and cuBLASLt's block-scaled NVFP4 GEMM
+    (torch._scaled_mm) alternating on the same operands, `warmup` + `steps` launches of each,
+    one event pair per launch; for profiler captures of the two kernels side by side."""
+    import torch
+    import blackhole_b200 as bh
+
+    A, SFA, sa = make_operand(M, K, 1, 1.0, dev)
+    B, SFB, sb = make_operand(N, K, 1000, 1.0, dev)
+    alpha = float(sa[1].item() * sb[1].item())
+    D = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+
+    def lib():
+        return torch._scaled_mm(A.view(torch.float4_e2m1fn_x2).view(M, K // 2),
+                                B.view(torch.float4_e2m1fn_x2).view(N, K // 2).t(),
+                                SFA.view(torch.float8_e4m3fn), SFB.view(torch.float8_e4m3fn),
+                                out_dtype=torch.bfloat16)
+
+    times = {"ours": [], "cublaslt": []}
+    for i in range(args.warmup + args.steps):
+        for name, fn in (("ours", lambda: bh.nvfp4_bf16_gemm(M, N, K, A, SFA, B, SFB, D, alpha)),
+                         ("cublaslt", lib)):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            if i >= args.warmup:
+                times[name].append((s, e))
+    torch.cuda.synchronize()
+    assert bh.device_status(torch.cuda.current_device()) == 0
+    us = {k: [round(s.elapsed_time(e) * 1e3, 1) for s, e in v] for k, v in times.items()}
+    return {"case": "compare", "shape": [M, N, K], "us_per_launch": us,
+            "gpu_launches": args.warmup + args.steps}
 
 
 # Decode legs warm up with ~0.1 s of decode launches: measured on B200, a decode timed right
@@ -887,6 +923,9 @@ def main():
             import torch.distributed as dist
             dist.barrier()
             dist.destroy_process_group()
+        return
+    if args.case == "compare":
+        print(json.dumps(run_compare(args, dev, M, N, K)), flush=True)
         return
     if args.case == "main":
         args.no_decode = True

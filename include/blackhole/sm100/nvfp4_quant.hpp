@@ -13,8 +13,8 @@
 //
 // This is the step before the GEMM that the reference performs on the host with CUTLASS
 // converters (example/nvfp4_bf16_gemm.cu:60-71, :104-133).  Two HBM-bound kernels:
-// a grid-stride amax reduction, then the quantiser proper with four lanes per 16-element
-// block (coalesced 512-byte warp loads, 64-byte warp stores of codes).
+// a grid-stride amax reduction, then the quantiser proper with two lanes per 16-element
+// block (a warp reads 1 KB of contiguous FP32 and stores 128 contiguous bytes of codes).
 // =====================================================================================
 
 #include <algorithm>
@@ -166,63 +166,85 @@ __device__ __forceinline__ float rcp_approx(float x) {
   return r;
 }
 
-template <class T> struct Vec4In;
-template <> struct Vec4In<float> {
-  static __device__ __forceinline__ float4 load(const float* p) {
-    return __ldcs(reinterpret_cast<const float4*>(p));
+// Eight consecutive elements of a lane (32 bytes of FP32 in two 16-byte loads that the same
+// warp's next load finds in L1, or one 16-byte load of BF16).
+template <class T> struct Vec8In;
+template <> struct Vec8In<float> {
+  static __device__ __forceinline__ void load(const float* p, float (&v)[8]) {
+    const float4 a = reinterpret_cast<const float4*>(p)[0];
+    const float4 b = reinterpret_cast<const float4*>(p)[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
   }
 };
-template <> struct Vec4In<__nv_bfloat16> {
-  static __device__ __forceinline__ float4 load(const __nv_bfloat16* p) {
-    const uint2 v = __ldcs(reinterpret_cast<const uint2*>(p));
-    return make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xFFFF0000u),
-                       __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xFFFF0000u));
+template <> struct Vec8In<__nv_bfloat16> {
+  static __device__ __forceinline__ void load(const __nv_bfloat16* p, float (&v)[8]) {
+    const uint4 q = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[2 * i] = __uint_as_float(w[i] << 16);
+      v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
   }
 };
 
-// Work item: 128 consecutive elements of one row (a segment), one warp, 4 elements per lane,
-// so one 16-element block is 4 neighbouring lanes.  Items run over the layout's padded rows
-// (a multiple of 128); items of padding rows and the groups past K of a row's last segment
-// write zero scale factors.  Every scale-factor write is one 4-byte word (4 groups of one row,
-// kg % 4 == 0 .. 3) by lane 0 or 16; codes are 16-bit stores, 64 contiguous bytes per warp.
-template <class T, int kUnroll>
+// Work item: 256 consecutive elements of one row (a segment), one warp, 8 elements per lane,
+// so one 16-element block is 2 neighbouring lanes.  Each warp takes a contiguous range of
+// items (row-major: segments of a row, then the next row), so it steps through rows without
+// dividing.  Items run over the layout's padded rows (a multiple of 128); items of padding
+// rows and the groups past K of a row's last segment write zero scale factors.  Every
+// scale-factor write is one 4-byte word (4 groups of one row) by lanes 0, 8, 16, 24; codes are
+// 32-bit stores, 128 contiguous bytes per warp.
+template <class T, int kItemsPerWarp>
 __global__ void __launch_bounds__(256) quantize_kernel(const T* __restrict__ x, int rows, int K,
                                                        uint8_t* __restrict__ packed,
                                                        uint8_t* __restrict__ sf,
                                                        float* __restrict__ scales) {
   const int lane = threadIdx.x & 31;
-  const int segs = (K + 127) / 128;
+  const int segs = (K + 255) / 256;
   const int rows_pad = (rows + 127) / 128 * 128;
   const int words_per_row = (K / 16 + 3) / 4;          // 4-group words (the padded groups)
   const int items = rows_pad * segs;                   // < 2^31: checked by the launcher
-  const int warp0 = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
-  const int nwarps = static_cast<int>((gridDim.x * blockDim.x) >> 5);
+  const int warp = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  int it = warp * kItemsPerWarp;
+  const int it_end = min(items, it + kItemsPerWarp);
   const float amax = scales[0];
   const float g = amax / 2688.0f;                       // amax / (448 * 6)
   if (blockIdx.x == 0 && threadIdx.x == 0) scales[1] = g;
   // (amax_b / 6) / g ~ amax_b * c: fl(1/6), fl(1/g) and their product, three roundings
   const float c = __frcp_rn(6.0f) * __frcp_rn(g);
-
-  for (int base = warp0 * kUnroll; base < items; base += nwarps * kUnroll) {
-    float4 v[kUnroll];
-    int row[kUnroll], k0[kUnroll];
-    bool live[kUnroll];
+  if (it >= it_end) return;
+  int r = it / segs;
+  int seg = it - r * segs;
+  constexpr int U = 2;                                  // items whose loads are in flight together
+  for (; it < it_end; it += U) {
+    float v[U][8];
+    int ru[U], k0[U];
+    bool live[U];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {          // every load of the unrolled items first
-      const int it = base + u;
-      const int r = it / segs;                    // warp-uniform
-      const int seg = it - r * segs;
-      row[u] = r;
-      k0[u] = seg * 128 + lane * 4;
-      live[u] = it < items && r < rows && k0[u] < K;
-      v[u] = live[u] ? Vec4In<T>::load(x + int64_t(r) * K + k0[u]) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int u = 0; u < U; ++u) {
+      ru[u] = r;
+      k0[u] = seg * 256 + lane * 8;
+      live[u] = it + u < it_end && r < rows && k0[u] < K;
+      if (live[u]) {
+        Vec8In<T>::load(x + int64_t(r) * K + k0[u], v[u]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[u][i] = 0.0f;
+      }
+      if (++seg == segs) {
+        seg = 0;
+        ++r;
+      }
     }
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      if (base + u >= items) break;               // warp-uniform
-      float m = fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)), fmaxf(fabsf(v[u].z), fabsf(v[u].w)));
-      m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
-      m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 2));   // the block's amax on its 4 lanes
+    for (int u = 0; u < U; ++u) {
+      if (it + u >= it_end) break;                      // warp-uniform
+      float m = fabsf(v[u][0]);
+#pragma unroll
+      for (int i = 1; i < 8; ++i) m = fmaxf(m, fabsf(v[u][i]));
+      m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));   // the block's amax on its 2 lanes
       uint32_t s_code = 0, codes = 0;
       if (live[u] && g > 0.0f && m > 0.0f) {
         const float ys = m * c;
@@ -231,26 +253,30 @@ __global__ void __launch_bounds__(256) quantize_kernel(const T* __restrict__ x, 
         if (s_val != 0.0f) {
           const float scale = s_val * g;
           const float rs = rcp_approx(scale);       // subnormal scale: inf, every y "near"
-          const float y0 = v[u].x * rs, y1 = v[u].y * rs, y2 = v[u].z * rs, y3 = v[u].w * rs;
-          if (near_e2m1_threshold(y0) || near_e2m1_threshold(y1) || near_e2m1_threshold(y2) ||
-              near_e2m1_threshold(y3))
-            codes = e2m1x4_cvt(v[u].x / scale, v[u].y / scale, v[u].z / scale, v[u].w / scale);
-          else
-            codes = e2m1x4_cvt(y0, y1, y2, y3);
+          float y[8];
+          bool near = false;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            y[i] = v[u][i] * rs;
+            near |= near_e2m1_threshold(y[i]);
+          }
+          if (near) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) y[i] = v[u][i] / scale;
+          }
+          codes = e2m1x4_cvt(y[0], y[1], y[2], y[3]) | (e2m1x4_cvt(y[4], y[5], y[6], y[7]) << 16);
         }
       }
-      if (live[u])
-        *reinterpret_cast<uint16_t*>(packed + (int64_t(row[u]) * K + k0[u]) / 2) =
-            static_cast<uint16_t>(codes);
-      // the 8 groups of the segment as two words: lanes 0, 4, 8, 12 and 16, 20, 24, 28
-      const int src = (lane & 16) + 4 * (lane & 3);
-      const uint32_t c = __shfl_sync(0xFFFFFFFFu, s_code, src) << (8 * (lane & 3));
-      uint32_t word = c;
-      word |= __shfl_xor_sync(0xFFFFFFFFu, word, 1);
+      if (live[u]) *reinterpret_cast<uint32_t*>(packed + (int64_t(ru[u]) * K + k0[u]) / 2) = codes;
+      // the 16 groups of the segment as four words: lanes 0, 2, 4, 6 -> word 0, lanes 8..14 ->
+      // word 1, ...; word w is assembled on lanes 8w..8w+3 and stored by lane 8w
+      const uint32_t cw = __shfl_sync(0xFFFFFFFFu, s_code, (lane & 24) + 2 * (lane & 3))
+                          << (8 * (lane & 3));
+      uint32_t word = cw | __shfl_xor_sync(0xFFFFFFFFu, cw, 1);
       word |= __shfl_xor_sync(0xFFFFFFFFu, word, 2);
-      const int w = (k0[u] - lane * 4) / 64 + (lane >> 4);   // this lane's word of the row
-      if ((lane & 15) == 0 && w < words_per_row)
-        *reinterpret_cast<uint32_t*>(sf + blackhole::sf_offset(row[u], 4 * w, K)) = word;
+      const int w = (k0[u] - lane * 8) / 64 + (lane >> 3);   // this lane's word of the row
+      if ((lane & 7) == 0 && w < words_per_row && ru[u] < rows_pad)
+        *reinterpret_cast<uint32_t*>(sf + blackhole::sf_offset(ru[u], 4 * w, K)) = word;
     }
   }
 }
@@ -372,23 +398,21 @@ inline cudaError_t nvfp4_quantize(const void* X, int x_is_bf16, int rows, int K,
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t n16 = int64_t(rows) * K / 16;
   const int amax_grid = static_cast<int>(std::min<int64_t>((n16 + 255) / 256, int64_t(sms) * 8));
-  // quantiser: 8 warps per CTA, 4 items (segments of 128 elements) per warp and pass,
-  // at most 8 CTAs per SM, striding over the items
-  constexpr int kUnroll = 4;
-  const int64_t items = (int64_t(rows) + 127) / 128 * 128 * ((K + 127) / 128);
+  // quantiser: 8 warps per CTA, each warp a contiguous range of kItems segments of 256
+  // elements (one pass over the tensor, ~10 warps per SM for the configs' shapes and more)
+  constexpr int kItems = 16;
+  const int64_t items = (int64_t(rows) + 127) / 128 * 128 * ((K + 255) / 256);
   if (items >= (int64_t(1) << 31) - (int64_t(1) << 20)) return cudaErrorInvalidValue;
-  const int qgrid = static_cast<int>(
-      std::max<int64_t>(1, std::min<int64_t>((items + 8 * kUnroll - 1) / (8 * kUnroll),
-                                             int64_t(sms) * 8)));
+  const int qgrid = static_cast<int>(std::max<int64_t>(1, (items + 8 * kItems - 1) / (8 * kItems)));
   if (x_is_bf16) {
     auto xp = static_cast<const __nv_bfloat16*>(X);
     quant_detail::amax_kernel<<<amax_grid, 256, 0, stream>>>(xp, n16, scales);
-    quant_detail::quantize_kernel<__nv_bfloat16, kUnroll><<<qgrid, 256, 0, stream>>>(
+    quant_detail::quantize_kernel<__nv_bfloat16, kItems><<<qgrid, 256, 0, stream>>>(
         xp, rows, K, static_cast<uint8_t*>(packed), static_cast<uint8_t*>(sf), scales);
   } else {
     auto xp = static_cast<const float*>(X);
     quant_detail::amax_kernel<<<amax_grid, 256, 0, stream>>>(xp, n16, scales);
-    quant_detail::quantize_kernel<float, kUnroll><<<qgrid, 256, 0, stream>>>(
+    quant_detail::quantize_kernel<float, kItems><<<qgrid, 256, 0, stream>>>(
         xp, rows, K, static_cast<uint8_t*>(packed), static_cast<uint8_t*>(sf), scales);
   }
   return cudaGetLastError();
