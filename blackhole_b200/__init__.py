@@ -151,17 +151,15 @@ def nvfp4_bf16_gemm(M: int, N: int, K: int, A, SFA, B, SFB, D, alpha: float = 1.
         raise BlackholeError("blackhole_sm100_nvfp4_bf16_gemm", rc)
 
 
-SCHEDULES = {"auto": 0, "1sm": 1, "2sm": 2, "skinny": 3, "skinny_noprefetch": 4,
-             "1sm_streamk": 5}
+SCHEDULES = {"auto": 0, "1sm": 1, "2sm": 2, "skinny": 3, "skinny_noprefetch": 4}
 
 
 def nvfp4_bf16_gemm_ex(M: int, N: int, K: int, A, SFA, B, SFB, D, alpha: float = 1.0,
                        schedule: str = "auto", workspace=None, workspace_bytes: int = 0,
                        stream=None) -> None:
     """nvfp4_bf16_gemm with an explicit schedule ("auto", "1sm", "2sm", "skinny",
-    "skinny_noprefetch": skinny without its early L2 prefetch, same results, "1sm_streamk": the
-    one-SM tiles split stream-K over every SM) and an optional caller-owned workspace for the
-    skinny and stream-K schedules (see workspace_bytes)."""
+    "skinny_noprefetch": skinny without its early L2 prefetch, same results) and an
+    optional caller-owned workspace for the skinny schedule (see workspace_bytes)."""
     if workspace is not None and hasattr(workspace, "numel") and not workspace_bytes:
         workspace_bytes = workspace.numel() * workspace.element_size()
     rc = load().blackhole_sm100_nvfp4_bf16_gemm_ex(

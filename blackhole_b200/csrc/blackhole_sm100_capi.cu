@@ -159,7 +159,7 @@ int blackhole_sm100_nvfp4_bf16_gemm_ex(int M, int N, int K, const void* A, const
                                        const void* B, const void* SFB, void* D, float alpha,
                                        int schedule, void* workspace, int64_t workspace_bytes,
                                        cudaStream_t stream) {
-  if (schedule < 0 || schedule > 5) return static_cast<int>(cudaErrorInvalidValue);
+  if (schedule < 0 || schedule > 4) return static_cast<int>(cudaErrorInvalidValue);
   return static_cast<int>(blackhole::sm100::nvfp4_bf16_gemm_ex(
       M, N, K, A, SFA, B, SFB, D, alpha, static_cast<blackhole::sm100::Nvfp4Schedule>(schedule),
       workspace, workspace_bytes, stream));
@@ -176,7 +176,7 @@ int blackhole_sm100_mxfp4_bf16_gemm_ex(int M, int N, int K, const void* A, const
                                        const void* B, const void* SFB, void* D, float alpha,
                                        int schedule, void* workspace, int64_t workspace_bytes,
                                        cudaStream_t stream) {
-  if (schedule < 0 || schedule > 5) return static_cast<int>(cudaErrorInvalidValue);
+  if (schedule < 0 || schedule > 4) return static_cast<int>(cudaErrorInvalidValue);
   return static_cast<int>(blackhole::sm100::mxfp4_bf16_gemm_ex(
       M, N, K, A, SFA, B, SFB, D, alpha, static_cast<blackhole::sm100::Nvfp4Schedule>(schedule),
       workspace, workspace_bytes, stream));
@@ -194,7 +194,7 @@ int blackhole_sm100_mxf8f4_bf16_gemm_ex(int M, int N, int K, const void* A, cons
                                         const void* B, const void* SFB, void* D, float alpha,
                                         int schedule, void* workspace, int64_t workspace_bytes,
                                         cudaStream_t stream) {
-  if (schedule < 0 || schedule > 5) return static_cast<int>(cudaErrorInvalidValue);
+  if (schedule < 0 || schedule > 4) return static_cast<int>(cudaErrorInvalidValue);
   return static_cast<int>(blackhole::sm100::mxf8f4_bf16_gemm_ex(
       M, N, K, A, SFA, B, SFB, D, alpha, static_cast<blackhole::sm100::Nvfp4Schedule>(schedule),
       workspace, workspace_bytes, stream));

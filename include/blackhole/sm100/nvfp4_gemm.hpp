@@ -52,7 +52,6 @@
 #include <utility>
 
 #include <blackhole/sm100/nvfp4_gemm_1sm.hpp>
-#include <blackhole/sm100/nvfp4_gemm_1sm_streamk.hpp>
 #include <blackhole/sm100/nvfp4_gemm_2sm.hpp>
 #include <blackhole/sm100/nvfp4_gemm_skinny.hpp>
 #endif
@@ -61,10 +60,7 @@ namespace blackhole::sm100 {
 
 // kSkinnyNoPrefetch is the skinny schedule without the L2 prefetch of B / SFB that it issues
 // while the previous kernel in the stream is finishing (same results; for measurement).
-// kOneSmStreamK is the one-SM tile split stream-K over every SM (for fewer tiles than SMs).
-enum class Nvfp4Schedule : int {
-  kAuto = 0, kOneSm = 1, kTwoSm = 2, kSkinny = 3, kSkinnyNoPrefetch = 4, kOneSmStreamK = 5
-};
+enum class Nvfp4Schedule : int { kAuto = 0, kOneSm = 1, kTwoSm = 2, kSkinny = 3, kSkinnyNoPrefetch = 4 };
 
 #if defined(__CUDACC__)
 
@@ -130,16 +126,6 @@ inline cudaError_t block_scaled_bf16_gemm_ex(int M, int N, int K, void const* A,
     case Nvfp4Schedule::kTwoSm:
       return detail::launch_2sm<Nvfp4Gemm2SmTraitsT<5, Fmt>>(M, N, K, A, SFA, B, SFB, D, alpha,
                                                               st, dev, stream);
-    case Nvfp4Schedule::kOneSmStreamK: {
-      const int64_t need = nvfp4_1sm_streamk_workspace_bytes(st->num_sms);
-      if (!workspace) {
-        e = detail::library_workspace(dev, stream, need, &workspace);
-        if (e != cudaSuccess) return e;
-        workspace_bytes = need;
-      }
-      return detail::launch_1sm_streamk<Nvfp4GemmTraitsT<4, Fmt>>(
-          M, N, K, A, SFA, B, SFB, D, alpha, workspace, workspace_bytes, st, dev, stream);
-    }
     case Nvfp4Schedule::kSkinny:
     case Nvfp4Schedule::kSkinnyNoPrefetch: {
       if (M > 128) return cudaErrorInvalidValue;
