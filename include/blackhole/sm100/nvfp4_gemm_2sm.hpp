@@ -59,11 +59,18 @@ struct Nvfp4Gemm2SmTraitsT {
   static constexpr int StageBytes = ABytes + BBytes + SFABytes + SFBBytes;
   static constexpr int StageTx = ATx + BTx + SFABytes + SFBBytes;
 
-  // NVFP4's scale factors take 24 KB of TMEM writes per k-tile (twice MXFP4's: 16-element
-  // blocks), more than hides behind the MMAs when the MMA warp issues the copies itself.  They
-  // are then copied by a warp of their own into SfBufs TMEM buffers, up to SfBufs k-tiles
-  // ahead of the MMAs (measured on B200 at 8192^3: 5% fewer cycles, 2.5% less time at the
-  // power cap; for MXFP4 the handoff costs more than it saves, so its MMA warp copies).
+  // NVFP4's scale factors take 12 tcgen05.cp per k-tile (twice MXFP4's: 16-element blocks)
+  // next to 4 MMAs and their commits.  All of them are issued by the leader CTA, and one warp
+  // issues a dependent tcgen05 instruction only every ~40-48 clocks, so a single warp cannot
+  // issue a k-tile's 19 instructions within the ~513 clocks its MMAs take.  The work is split
+  // between two warps: a copy warp copies SFB and the last SFA atom into SfBufs TMEM buffers,
+  // up to SfBufs k-tiles ahead of the MMAs, and the MMA warp copies the other MmaSfaAtoms SFA
+  // atoms itself, in order, right before the k-tile's MMAs (11 and 9 instructions per k-tile).
+  // The stage's scale factors are loaded first and land on a barrier of their own, so the copy
+  // warp need not wait for the stage's A and B.  Measured on B200 at 8192^3, back to back:
+  // all 12 copies in the copy warp 231 us, this split 216 us; all 12 in the MMA warp was ~5%
+  // slower than the copy warp, and two copy warps slower still.  For MXFP4 the handoff costs
+  // more than it saves, so its MMA warp copies everything.
   //
   // OverlapAcc: two accumulator stages that share AccOverlap columns of TMEM (stage s at
   // column s * AccStageStride), one tile per stage in turn, and one scale-factor buffer after
@@ -82,6 +89,7 @@ struct Nvfp4Gemm2SmTraitsT {
   static constexpr int FirstEpiWarp = 2;
   static constexpr int NumEpiWarps = 8;
   static constexpr int SfWarp = 10;              // (SfCopyWarp only)
+  static constexpr int MmaSfaAtoms = SfCopyWarp ? SfAtoms - 1 : 0;   // SFA atoms the MMA warp copies
 
   // TMEM columns: accumulator [0,256); scale factors after it: SFA (4 columns per k-step)
   // then SFB (8 per k-step).
@@ -95,8 +103,10 @@ struct Nvfp4Gemm2SmTraitsT {
   static constexpr int StagingBytes = NumEpiWarps * StoreBoxBytes;
 
   // stage full/empty, accumulator full/empty, drain, TMEM slot + abort flag, then (copy warp)
-  // scale-factor buffer full/empty and the copy warp's drain barrier
-  static constexpr int BarrierBytes = 8 * (2 * Stages + 4) + 16 + 8 * (2 * SfBufs + 1);
+  // scale-factor buffer full/empty, the copy warp's drain barrier and the stages' scale-factor
+  // full barriers
+  static constexpr int BarrierBytes =
+      8 * (2 * Stages + 4) + 16 + 8 * (2 * SfBufs + 1) + (SfCopyWarp ? 8 * Stages : 0);
   static constexpr int SmemBytes = Stages * StageBytes + StagingBytes + BarrierBytes + 1024;
 
   static_assert(SmemBytes <= arch_traits<Arch::kSm100>::max_smem_per_cta, "smem budget");
@@ -191,6 +201,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
   const uint32_t sf_full0 = bars + 16u * S + 48u;                 // + 8 b, b < SfBufs
   const uint32_t sf_empty0 = sf_full0 + 8u * KT::SfBufs;          // + 8 b
   const uint32_t sf_drain = sf_full0 + 16u * KT::SfBufs;
+  // (copy warp) the stage's scale factors have landed; without a copy warp full_bar covers them
+  auto sf_bar = [&](int s) { return KT::SfCopyWarp ? sf_drain + 8u + 8u * s : full_bar(s); };
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -213,6 +225,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
         mbar_init(sf_empty0 + 8u * b, 1);
       }
       mbar_init(sf_drain, 1);
+      for (int s = 0; s < S; ++s) mbar_init(sf_bar(s), 1);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -258,13 +271,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
             break;
           }
           const uint32_t lb = mapa_shared(full_bar(stage), 0);
-          if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), 2u * KT::StageTx);
+          const uint32_t ls = mapa_shared(sf_bar(stage), 0);
+          if (rank == 0) {
+            if constexpr (KT::SfCopyWarp) {
+              mbar_arrive_expect_tx(sf_bar(stage), 2u * (KT::SFABytes + KT::SFBBytes));
+              mbar_arrive_expect_tx(full_bar(stage), 2u * (KT::ATx + KT::BTx));
+            } else {
+              mbar_arrive_expect_tx(full_bar(stage), 2u * KT::StageTx);
+            }
+          }
+          // scale factors first (the copy warp waits for them alone), one request per
+          // operand: SFA as one 2 KB row, SFB as the pair's two 2 KB rows
+          const int sf_y = p.sf_tail ? KT::SfAtoms * kt : kt;
+          tma_load_3d_pair(sSFA + stage * KT::SFABytes, &p.tmap_sfa, ls, 0, sf_y, sfa_blk, pol);
+          tma_load_3d_pair(sSFB + stage * KT::SFBBytes, &p.tmap_sfb, ls, 0, sf_y, sfb_blk, pol);
           tma_load_2d_pair(sA + stage * KT::ABytes, &p.tmap_a, lb, kt * KT::RowBytes, a_row, pol);
           tma_load_2d_pair(sB + stage * KT::BBytes, &p.tmap_b, lb, kt * KT::RowBytes, b_row, pol);
-          // one request per operand: SFA as one 2 KB row, SFB as the pair's two 2 KB rows
-          const int sf_y = p.sf_tail ? KT::SfAtoms * kt : kt;
-          tma_load_3d_pair(sSFA + stage * KT::SFABytes, &p.tmap_sfa, lb, 0, sf_y, sfa_blk, pol);
-          tma_load_3d_pair(sSFB + stage * KT::SFBBytes, &p.tmap_sfb, lb, 0, sf_y, sfb_blk, pol);
           ++issued;
           if (++stage == S) {
             stage = 0;
@@ -277,6 +299,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
           if (issued > s) {
             const int64_t cnt = (issued - 1 - s) / S + 1;
             detail::drain_wait(full_bar(s), uint32_t((cnt - 1) & 1));
+            if (KT::SfCopyWarp) detail::drain_wait(sf_bar(s), uint32_t((cnt - 1) & 1));
           }
         }
       }
@@ -347,12 +370,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
           const uint32_t ready = more ? mbar_probe(full_bar(nstage), nphase) : 1u;
           if constexpr (KT::SfCopyWarp) {
             sfbuf = uint32_t(nkt % KT::SfBufs);
+            // the copy warp's share of buffer sfbuf is in TMEM (it waited for the stage's
+            // scale factors); the stage's own barrier is acquired here too (already complete)
+            // before this warp copies the first MmaSfaAtoms SFA atoms, in order before the MMAs
             if (!wait_bounded_warp(sf_full0 + 8u * sfbuf, uint32_t((nkt / KT::SfBufs) & 1),
-                                   abort_flag, p.status, kStatusMmaTimeout)) {
+                                   abort_flag, p.status, kStatusMmaTimeout) ||
+                !wait_bounded_warp(sf_bar(stage), phase, abort_flag, p.status, kStatusMmaTimeout)) {
               ok = false;
               break;
             }
             tc_fence_after();
+            const uint32_t sfa_s = sSFA + stage * KT::SFABytes;
+            const uint32_t ta0 = tmem + KT::SfCol + KT::SfStride * sfbuf;
+#pragma unroll
+            for (int j = 0; j < KT::MmaSfaAtoms; ++j)
+              tc_cp_32x128b_warpx4_pair_w(ta0 + 4 * j, desc_sf_atom(sfa_s + 512 * j));
           } else if (!KT::OverlapAcc || kt > 0) {
             copy_sf(stage, sfbuf);
           }
@@ -398,7 +430,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
   } else if (KT::SfCopyWarp && warp == KT::SfWarp) {
     // ------------------------------ scale-factor copier (leader CTA) ----------------
     // k-tile n: wait until the MMAs of k-tile n - SfBufs have released TMEM buffer n % SfBufs
-    // and stage n's loads have landed, copy its scale factors into that buffer, commit.
+    // and stage n's scale factors have landed, copy its SFB and its last SFA atoms (the MMA
+    // warp copies the first MmaSfaAtoms) into that buffer, commit.
     if (rank == 0) {
       int stage = 0;
       uint32_t phase = 0;
@@ -409,7 +442,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
           const uint32_t b = uint32_t(nkt % KT::SfBufs);
           if (!wait_bounded_warp(sf_empty0 + 8u * b, uint32_t(((nkt / KT::SfBufs) & 1) ^ 1),
                                  abort_flag, p.status, kStatusMmaTimeout) ||
-              !wait_bounded_warp(full_bar(stage), phase, abort_flag, p.status, kStatusMmaTimeout)) {
+              !wait_bounded_warp(sf_bar(stage), phase, abort_flag, p.status, kStatusMmaTimeout)) {
             ok = false;
             break;
           }
@@ -419,7 +452,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
           const uint32_t ta = tmem + KT::SfCol + KT::SfStride * b;
 #pragma unroll
           for (int j = 0; j < KT::SfAtoms; ++j) {
-            tc_cp_32x128b_warpx4_pair_w(ta + 4 * j, desc_sf_atom(sfa_s + 512 * j));
+            if (j >= KT::MmaSfaAtoms)
+              tc_cp_32x128b_warpx4_pair_w(ta + 4 * j, desc_sf_atom(sfa_s + 512 * j));
             tc_cp_32x128b_warpx4_pair_w(ta + 4 * KT::SfAtoms + 8 * j, desc_sf_atom(sfb_s + 512 * j));
             tc_cp_32x128b_warpx4_pair_w(ta + 4 * KT::SfAtoms + 8 * j + 4,
                                         desc_sf_atom(sfb_s + KT::SFBBytes / 2 + 512 * j));
