@@ -8,10 +8,12 @@
 //
 //   * CTA r of the pair loads rows [128r, 128r+128) of the A tile and of the B tile, its
 //     own 128 rows of SFA and all 256 rows of SFB (TMA, 128B swizzle for A/B) into a
-//     5-stage ring of 38 KB stages.  Every load of either CTA completes on the leader CTA's
-//     "full" barrier (TMA .cta_group::2), which expects the bytes of both CTAs.
-//   * The leader's MMA warp copies both CTAs' scale factors to their TMEM
-//     (tcgen05.cp.cta_group::2) and issues the MMAs, which read A/B halves from both CTAs'
+//     5-stage ring of 38 KB stages.  Every load of either CTA completes on a barrier of the
+//     leader CTA (TMA .cta_group::2) that expects the bytes of both CTAs: "full" for A / B,
+//     and for NVFP4 a separate scale-factor barrier per stage (its loads are issued first).
+//   * The leader copies both CTAs' scale factors to their TMEM (tcgen05.cp.cta_group::2;
+//     for NVFP4 split between a copy warp and the MMA warp, see the traits), and its MMA
+//     warp issues the MMAs, which read A/B halves from both CTAs'
 //     shared memory and write each CTA's 128 x 256 FP32 accumulator into its own TMEM.
 //     Its commits arrive on the "empty" barriers of both CTAs and, per tile, on both CTAs'
 //     "acc_full" barriers.
