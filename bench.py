@@ -103,7 +103,7 @@ class ClockSampler:
     REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
                "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, device_index, interval=0.001):
+    def __init__(self, device_index, interval=0.0002):
         self.samples, self.reasons = [], set()
         self.max_mhz = None
         self._stop = threading.Event()
