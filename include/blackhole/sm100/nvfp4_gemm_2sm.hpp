@@ -359,7 +359,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
           }
           tc_fence_after();
           // the first stage of a tile is waited for; each later one is probed one k-tile ahead
-          if (!wait_bounded_warp(full_bar(stage), phase, abort_flag, p.status, kStatusMmaTimeout)) {
+          // (A / B and, with the copy warp, the stage's own scale-factor barrier: this warp
+          // copies part of SFA from it)
+          if (!wait_bounded_warp(full_bar(stage), phase, abort_flag, p.status, kStatusMmaTimeout) ||
+              (KT::SfCopyWarp &&
+               !wait_bounded_warp(sf_bar(stage), phase, abort_flag, p.status, kStatusMmaTimeout))) {
             ok = false;
             break;
           }
@@ -369,15 +373,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
           const int nstage = stage + 1 == S ? 0 : stage + 1;
           const uint32_t nphase = stage + 1 == S ? (phase ^ 1u) : phase;
           const bool more = kt + 1 < p.k_tiles;
-          const uint32_t ready = more ? mbar_probe(full_bar(nstage), nphase) : 1u;
+          // (a probe issued here is consumed after the MMAs, so its latency stays off the issue
+          // chain; a second blocking wait per k-tile measured ~4% slower at 8192^3)
+          const uint32_t ready =
+              more ? mbar_probe(full_bar(nstage), nphase) &
+                         (KT::SfCopyWarp ? mbar_probe(sf_bar(nstage), nphase) : 1u)
+                   : 1u;
           if constexpr (KT::SfCopyWarp) {
             sfbuf = uint32_t(nkt % KT::SfBufs);
-            // the copy warp's share of buffer sfbuf is in TMEM (it waited for the stage's
-            // scale factors); the stage's own barrier is acquired here too (already complete)
-            // before this warp copies the first MmaSfaAtoms SFA atoms, in order before the MMAs
+            // the copy warp's share of buffer sfbuf is in TMEM; this warp copies the first
+            // MmaSfaAtoms SFA atoms itself, in order before the MMAs (the stage's scale-factor
+            // barrier was acquired with its A / B one k-tile ahead)
             if (!wait_bounded_warp(sf_full0 + 8u * sfbuf, uint32_t((nkt / KT::SfBufs) & 1),
-                                   abort_flag, p.status, kStatusMmaTimeout) ||
-                !wait_bounded_warp(sf_bar(stage), phase, abort_flag, p.status, kStatusMmaTimeout)) {
+                                   abort_flag, p.status, kStatusMmaTimeout)) {
               ok = false;
               break;
             }
@@ -411,7 +419,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KT::NumThreads, 1)
           phase = nphase;
           if (more) {
             if (!__all_sync(0xFFFFFFFFu, ready != 0u) &&
-                !wait_bounded_warp(full_bar(stage), phase, abort_flag, p.status, kStatusMmaTimeout)) {
+                (!wait_bounded_warp(full_bar(stage), phase, abort_flag, p.status, kStatusMmaTimeout) ||
+                 (KT::SfCopyWarp &&
+                  !wait_bounded_warp(sf_bar(stage), phase, abort_flag, p.status, kStatusMmaTimeout)))) {
               ok = false;
               break;
             }
