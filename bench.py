@@ -217,9 +217,11 @@ def gemm_bytes(M, N, K):
     return M * K // 2 + N * K // 2 + M * K // 16 + N * K // 16 + 2 * M * N
 
 
-def time_gemm(M, N, K, sets, D, steps, warmup, world, schedule="auto", fmt="nvfp4"):
+def time_gemm(M, N, K, sets, D, steps, warmup, world, schedule="auto", fmt="nvfp4", clk=None):
     """Back-to-back launches cycling through the input sets; returns total ms of `steps`
-    launches from CUDA events on the launching stream (one event pair around all of them)."""
+    launches from CUDA events on the launching stream (one event pair around all of them).
+    A ClockSampler passed as `clk` samples exactly the timed region (after the warm-up
+    barrier, until the closing one)."""
     import torch
     import blackhole_b200 as bh
 
@@ -238,15 +240,21 @@ def time_gemm(M, N, K, sets, D, steps, warmup, world, schedule="auto", fmt="nvfp
     for i in range(warmup):
         launch(*sets[i % len(sets)])
     barrier(world)
-    s = torch.cuda.Event(enable_timing=True)
-    e = torch.cuda.Event(enable_timing=True)
-    s.record(stream)
-    h0 = time.perf_counter()
-    for i in range(steps):
-        launch(*sets[i % len(sets)])
-    host_us = (time.perf_counter() - h0) * 1e6 / steps
-    e.record(stream)
-    barrier(world)
+    if clk is not None:
+        clk.__enter__()
+    try:
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        h0 = time.perf_counter()
+        for i in range(steps):
+            launch(*sets[i % len(sets)])
+        host_us = (time.perf_counter() - h0) * 1e6 / steps
+        e.record(stream)
+        barrier(world)
+    finally:
+        if clk is not None:
+            clk.__exit__(None, None, None)
     time_gemm.host_us_per_launch = host_us
     return s.elapsed_time(e)
 
@@ -941,8 +949,8 @@ def main():
     D = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.int32, device=dev)
 
-    with ClockSampler(torch.cuda.current_device()) as clk:
-        total_ms = time_gemm(M, N, K, sets, D, args.steps, args.warmup, world, args.schedule)
+    clk = ClockSampler(torch.cuda.current_device())
+    total_ms = time_gemm(M, N, K, sets, D, args.steps, args.warmup, world, args.schedule, clk=clk)
     fsteps = min(args.steps, 20)
     ftimes = time_gemm_flushed(M, N, K, A, SFA, B, SFB, D, alpha, fsteps, flush, world)
     assert bh.device_status(torch.cuda.current_device()) == 0
