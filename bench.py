@@ -103,11 +103,17 @@ class ClockSampler:
     REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
                "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, device_index, interval=0.0002):
+    def __init__(self, device_index, interval=0.0002, enabled=True):
+        """enabled=False (ranks other than 0, whose record is not printed) samples nothing:
+        eight ranks querying NVML at once slow each other down to ~1 sample per timed region."""
         self.samples, self.reasons = [], set()
         self.max_mhz = None
         self._stop = threading.Event()
         self._thr = None
+        self.nv = None
+        if not enabled:
+            self.interval = interval
+            return
         try:
             import pynvml as nv
             nv.nvmlInit()
@@ -167,6 +173,12 @@ def dist_setup(args):
     elif torch.cuda.is_available():
         torch.cuda.set_device(0)
     return world, rank, local
+
+
+def dist_rank():
+    """This process's rank (0 without a process group)."""
+    import torch.distributed as dist
+    return dist.get_rank() if dist.is_available() and dist.is_initialized() else 0
 
 
 def max_over_ranks(x, world):
@@ -469,7 +481,7 @@ def library_baseline(M, N, K, sets, steps, warmup, world):
         launch(*sets[i % len(sets)])
     barrier(world)
     time.sleep(1.0)  # let the power limiter settle as before our own timed region
-    with ClockSampler(torch.cuda.current_device()) as clk:
+    with ClockSampler(torch.cuda.current_device(), enabled=not dist_rank()) as clk:
         s = torch.cuda.Event(enable_timing=True)
         e = torch.cuda.Event(enable_timing=True)
         s.record()
@@ -910,7 +922,7 @@ def main():
     fp4_peak = 4.0 * bf16_peak
     M, N, K = args.m, args.n, args.k
     if args.case == "decode":
-        with ClockSampler(torch.cuda.current_device()) as clk:
+        with ClockSampler(torch.cuda.current_device(), enabled=rank == 0) as clk:
             d = run_decode(args, dev, rank, world, hbm_peak, peak_src)
         assert bh.device_status(torch.cuda.current_device()) == 0
         if rank == 0:
@@ -949,7 +961,7 @@ def main():
     D = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.int32, device=dev)
 
-    clk = ClockSampler(torch.cuda.current_device())
+    clk = ClockSampler(torch.cuda.current_device(), enabled=rank == 0)
     total_ms = time_gemm(M, N, K, sets, D, args.steps, args.warmup, world, args.schedule, clk=clk)
     fsteps = min(args.steps, 20)
     ftimes = time_gemm_flushed(M, N, K, A, SFA, B, SFB, D, alpha, fsteps, flush, world)
