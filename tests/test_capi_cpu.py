@@ -137,3 +137,20 @@ def test_peer_barrier_null_or_misaligned_flags_rejected():
         with pytest.raises(bh.BlackholeError) as ei:
             bh.peer_barrier(flags, 2, 0, 1, 10**9, stream=0)
         assert ei.value.code == 1
+
+
+@pytest.mark.parametrize("schedule", [-1, 5, 6, 1 << 20])
+@pytest.mark.parametrize("entry", ["blackhole_sm100_nvfp4_bf16_gemm_ex",
+                                   "blackhole_sm100_mxfp4_bf16_gemm_ex",
+                                   "blackhole_sm100_mxf8f4_bf16_gemm_ex"])
+def test_ex_rejects_unknown_schedules(entry, schedule):
+    """Schedules are 0 (by shape) to 4; anything else is cudaErrorInvalidValue before any
+    device work (valid shapes and aligned pointers, so only the schedule is wrong)."""
+    import ctypes
+    fn = getattr(bh.load(), entry)
+    good = 1 << 20
+    rc = fn(ctypes.c_int(128), ctypes.c_int(128), ctypes.c_int(256),
+            *(ctypes.c_void_p(good) for _ in range(5)), ctypes.c_float(1.0), ctypes.c_int(schedule),
+            ctypes.c_void_p(0), ctypes.c_int64(0), ctypes.c_void_p(0))
+    assert rc == 1
+    assert set(bh.SCHEDULES.values()) == set(range(5))
