@@ -69,6 +69,30 @@ def test_alpha_scales_output():
         assert bad == 0
 
 
+@pytest.mark.parametrize("schedule,M,N,K", [("skinny", 16, 1024, 512), ("1sm", 128, 512, 512),
+                                            ("2sm", 512, 512, 512)])
+def test_alpha_edge_values(schedule, M, N, K):
+    """alpha = +-0 (signed zeros out); +-1e32 (alpha * acc straddles the top of the BF16 range:
+    most results round to +-inf, the rest stay finite); 3e37 (alpha * acc overflows FP32);
+    1e-44 (an FP32 subnormal alpha: subnormal and zero BF16 results) through each schedule's
+    epilogue.  Zeros and infinities must match the oracle bit for bit, finite values the usual
+    tolerance."""
+    A, SFA, B, SFB, _ = C.make_operands(M, N, K, seed=21 + M)
+    for alpha in (0.0, -0.0, 1e32, -1e32, 3e37, 1e-44):
+        got = C.run_gpu(M, N, K, A, SFA, B, SFB, alpha, schedule=schedule)
+        ref, ad = O.gemm_full(M, N, K, A, SFA, B, SFB, alpha)
+        rf, gf = O.bf16_bits_to_f32(ref.ravel()), O.bf16_bits_to_f32(got.ravel())
+        special = ~np.isfinite(rf) | ~np.isfinite(gf) | (rf == 0) | (gf == 0)
+        assert np.array_equal(got.ravel()[special], ref.ravel()[special]), f"alpha={alpha}"
+        if abs(alpha) >= 1e32:
+            assert np.isinf(rf).any(), "the case must reach the overflow"
+        if alpha == 0.0:
+            assert np.array_equal(got, ref), "signed zeros"
+        fin = ~special
+        bad, *_ = O.check(ref.ravel()[fin], got.ravel()[fin], alpha, K, ad.ravel()[fin])
+        assert bad == 0, f"alpha={alpha}: {bad} finite elements outside tolerance"
+
+
 def test_outlier_activations_config3_style():
     M, N, K = 256, 512, 2048
     A, SFA, B, SFB, alpha = C.make_operands(M, N, K, seed=3, std_b=0.02, outlier_p=0.01)
