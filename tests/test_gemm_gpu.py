@@ -93,6 +93,26 @@ def test_alpha_edge_values(schedule, M, N, K):
         assert bad == 0, f"alpha={alpha}: {bad} finite elements outside tolerance"
 
 
+@pytest.mark.parametrize("schedule,M,N,K", [("skinny", 16, 1024, 1024), ("1sm", 128, 512, 1024),
+                                            ("2sm", 512, 512, 1024)])
+def test_full_range_codes_and_scale_factors(schedule, M, N, K):
+    """Every E2M1 code (signed zero included) and UE4M3 scale factors drawn from the whole
+    finite range (codes 0..126: zero, 2^-9 .. 448), not the quantiser's narrow band: products
+    span ~2^-20 .. 2^22, so the FP32 sums see large cancellations and rounding differences of
+    order; the result must stay within the stated tolerance of the oracle."""
+    rng = np.random.default_rng(1000 + M)
+    A = rng.integers(0, 256, M * K // 2, dtype=np.uint8)
+    B = rng.integers(0, 256, N * K // 2, dtype=np.uint8)
+    SFA = np.zeros(O.sf_storage_bytes(M, K), dtype=np.uint8)
+    SFB = np.zeros(O.sf_storage_bytes(N, K), dtype=np.uint8)
+    SFA[O.sf_offsets(M, K).ravel()] = rng.integers(0, 127, M * (K // 16), dtype=np.uint8)
+    SFB[O.sf_offsets(N, K).ravel()] = rng.integers(0, 127, N * (K // 16), dtype=np.uint8)
+    got = C.run_gpu(M, N, K, A, SFA, B, SFB, 1.0, schedule=schedule)
+    (bad, maxerr, ratio, _), ref = C.check_full(M, N, K, A, SFA, B, SFB, 1.0, got)
+    assert bad == 0, f"{bad} elements outside tolerance (max err {maxerr}, err/tol {ratio})"
+    assert np.isfinite(O.bf16_bits_to_f32(ref.ravel())).all()
+
+
 def test_outlier_activations_config3_style():
     M, N, K = 256, 512, 2048
     A, SFA, B, SFB, alpha = C.make_operands(M, N, K, seed=3, std_b=0.02, outlier_p=0.01)
