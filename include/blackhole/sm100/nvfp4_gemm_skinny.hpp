@@ -80,8 +80,9 @@ struct Nvfp4SkinnyTraits {
   // k-tiles' worth of weight rows in every format
   static constexpr int L2PrefetchKTiles = 20 / KPS;
   // ranges by ticket: the first CTA to start gets (1 + s) x, the last (1 - s) x the mean
-  // work, s = RangeSkew / 64
-  static constexpr int RangeSkew = 6;
+  // work, s = RangeSkew / 64 (measured on B200 at M = 16, N = 28672, K = 8192, back to back,
+  // medians of six: skew 6 / 8 / 9 / 10 took 24.14 / 23.78 / 23.75 / 23.92 us, 0 took ~25.5)
+  static constexpr int RangeSkew = MPAD <= 16 ? 9 : 6;
 
   // TMA, MMA, then 4 epilogue warps (one per TMEM sub-partition), or 8 for MPAD >= 64: two per
   // sub-partition, each draining half of the accumulator columns (the last segment's
