@@ -349,6 +349,22 @@ inline DeviceState* prepare_device() {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  // The tensor-map encoder is a driver call and needs a context current on this host thread.
+  // A thread whose only CUDA calls so far were ones that bind none (cudaGetDevice, cached
+  // set-up) has none, and the encoder then fails (seen: a new thread's first one-SM call after
+  // another thread had done the per-device set-up).  cudaFree(nullptr) does nothing but make
+  // the runtime bind the device's primary context, or keep the one the thread already has;
+  // once per thread and device.
+  thread_local uint64_t bound = 0;
+  if (!(bound & (uint64_t(1) << dev))) {
+    e = cudaFree(nullptr);
+    if (e != cudaSuccess) {
+      thread_local DeviceState unbound;
+      unbound.init_err = e;
+      return &unbound;
+    }
+    bound |= uint64_t(1) << dev;
+  }
   DeviceState& st = device_state(dev);
   std::lock_guard<std::mutex> lock(st.mu);
   if (st.ready) return &st;
