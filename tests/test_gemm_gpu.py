@@ -113,6 +113,18 @@ def test_full_range_codes_and_scale_factors(schedule, M, N, K):
     assert np.isfinite(O.bf16_bits_to_f32(ref.ravel())).all()
 
 
+@pytest.mark.parametrize("schedule,M,N,K", [("skinny", 16, 1024, 65536), ("1sm", 128, 512, 65536),
+                                            ("2sm", 512, 512, 65536)])
+def test_long_k(schedule, M, N, K):
+    """K = 65536, past every config (configs[3] has K = 28672): 256 k-tiles of FP32 accumulation
+    per output, and the K-dependent index arithmetic (k-tile coordinates, scale-factor atoms,
+    stream-K units) at twice the configs' range; sampled against the oracle."""
+    A, SFA, B, SFB, alpha = C.make_operands(M, N, K, seed=77 + M, std_b=0.02)
+    got = C.run_gpu(M, N, K, A, SFA, B, SFB, alpha, schedule=schedule)
+    bad, maxerr, ratio, rel = C.check_sampled(M, N, K, A, SFA, B, SFB, alpha, got, S=2048)
+    assert bad == 0, f"{bad} bad (max err {maxerr}, err/tol {ratio})"
+
+
 def test_outlier_activations_config3_style():
     M, N, K = 256, 512, 2048
     A, SFA, B, SFB, alpha = C.make_operands(M, N, K, seed=3, std_b=0.02, outlier_p=0.01)
