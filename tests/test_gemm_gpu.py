@@ -125,6 +125,42 @@ def test_long_k(schedule, M, N, K):
     assert bad == 0, f"{bad} bad (max err {maxerr}, err/tol {ratio})"
 
 
+@pytest.mark.parametrize("schedule,M,N,K", [("skinny", 16, 1024, 2048), ("1sm", 128, 512, 1024),
+                                            ("2sm", 512, 512, 1024)])
+def test_operands_only_16_byte_aligned(schedule, M, N, K):
+    """Callers pass slices of larger tensors: every operand (A, SFA, B, SFB, D) starts 16 bytes
+    into a buffer, the least alignment the entry points accept, and no kernel may assume more."""
+    import torch
+    import blackhole_b200 as bh
+
+    A, SFA, B, SFB, alpha = C.make_operands(M, N, K, seed=88 + M, std_b=0.02)
+    dev = torch.device("cuda:0")
+
+    def at16(x):
+        buf = torch.zeros(x.size + 64, dtype=torch.uint8, device=dev)
+        view = buf[16:16 + x.size]
+        view.copy_(torch.from_numpy(x.ravel()))
+        assert view.data_ptr() % 128 == 16
+        return view
+
+    tA, tSFA, tB, tSFB = (at16(x) for x in (A, SFA, B, SFB))
+    dbuf = torch.full((M * N + 32,), float("nan"), dtype=torch.bfloat16, device=dev)
+    D = dbuf[8:8 + M * N]          # 16 bytes in
+    assert D.data_ptr() % 128 == 16
+    if schedule == "auto":
+        bh.nvfp4_bf16_gemm(M, N, K, tA, tSFA, tB, tSFB, D, alpha)
+    else:
+        bh.nvfp4_bf16_gemm_ex(M, N, K, tA, tSFA, tB, tSFB, D, alpha, schedule=schedule)
+    torch.cuda.synchronize()
+    assert bh.device_status(0) == 0
+    got = D.view(torch.int16).cpu().numpy().view(np.uint16).reshape(M, N)
+    ref, ad = O.gemm_full(M, N, K, A, SFA, B, SFB, alpha)
+    bad, maxerr, ratio, _ = O.check(ref, got, alpha, K, ad)
+    assert bad == 0, f"{bad} elements outside tolerance (err/tol {ratio})"
+    assert np.isnan(dbuf[:8].float().cpu().numpy()).all(), "wrote before D"
+    assert np.isnan(dbuf[8 + M * N:].float().cpu().numpy()).all(), "wrote past D"
+
+
 def test_outlier_activations_config3_style():
     M, N, K = 256, 512, 2048
     A, SFA, B, SFB, alpha = C.make_operands(M, N, K, seed=3, std_b=0.02, outlier_p=0.01)
